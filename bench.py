@@ -1,0 +1,496 @@
+"""Decode-step benchmark of the B200 KV selection-and-offload path.
+
+Workload (Qwen2.5-VL-7B decode selection): 28 layers, 28 query / 4 KV heads, head_dim 128,
+bf16; 8 sequences per GPU of 16384 tokens (first 75% ~N(0,1) "image" KV, rest ~N(0,0.5));
+all K and V in pinned host memory, K also in HBM key pages for scoring; q ~N(0,1).
+One step = one decode step over all 28 layers: GQA-summed scores -> top-2048 of the
+non-window tokens ∪ the last 128 per (sequence, KV head) -> UVA gather of the selected K/V
+rows from host memory into HBM -> attention over them.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mserve|reference]
+
+Prints one JSON line (rank 0).  value = selected K+V bytes gathered host->HBM per second over
+the whole step (all ranks), ms_per_step = decode-step time (max over ranks).  With N > 1
+(torchrun) every rank serves its own 8 sequences over its own host link; there is no
+collective on the data path (weak scaling).  --impl reference times the C restatement of the
+reference's CPU path (oracle/oracle_kv.c: scores, selection, index_select gather + the H2D
+copy of the gathered rows, attention) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "selected-KV gather GB/s host→HBM vs PCIe peak; decode step ms at 1/2/4/8 B200"
+WORKLOAD = dict(layers=28, batch=8, q_heads=28, kv_heads=4, head_dim=128, seq_len=16384, top_k=2048, recent=128,
+                image_frac=0.75)
+WORKLOAD_NAME = ("qwen2.5-vl-7b decode selection: 28 layers, 28q/4kv heads, head_dim 128, bf16, 8 seqs x 16384 "
+                 "tokens per GPU, top-2048 + last-128 per (seq, kv head), KV in pinned host")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["mserve", "reference"], default="mserve")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count (smaller test runs only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------- helpers
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            p = [x.strip() for x in l.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def pcie_peaks(device, nbytes=256 << 20, reps=5):
+    """Pinned cudaMemcpyAsync H2D / D2H peak of this GPU's host link (GB/s, best of reps)."""
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    g = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    out = {}
+    for name in ("h2d", "d2h"):
+        best = 0.0
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            if name == "h2d":
+                g.copy_(h, non_blocking=True)
+            else:
+                h.copy_(g, non_blocking=True)
+            e1.record()
+            e1.synchronize()
+            best = max(best, nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+        out[name] = best
+    del h, g
+    return out
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            pass
+    return {}
+
+
+def ncu_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary (None if absent)."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(kernel)
+    except ValueError:
+        return None
+
+
+# ------------------------------------------------------------------------------------- workload
+def build_engine(wl, device, seed):
+    from mserve_b200.engine import OffloadKV
+    L, B, Hq, Hkv, D, T = (wl[k] for k in ("layers", "batch", "q_heads", "kv_heads", "head_dim", "seq_len"))
+    eng = OffloadKV(L, B, Hq, Hkv, D, T + 256, top_k=wl["top_k"], recent=wl["recent"], device=device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    n_img = int(T * wl["image_frac"])
+    eng.reserve([T] * B)
+    for layer in range(L):
+        k = torch.randn(B, Hkv, T, D, generator=g, device=device, dtype=torch.float32)
+        v = torch.randn(B, Hkv, T, D, generator=g, device=device, dtype=torch.float32)
+        k[:, :, n_img:] *= 0.5
+        v[:, :, n_img:] *= 0.5
+        eng.append_layer(layer, k.to(torch.bfloat16), v.to(torch.bfloat16))
+        del k, v
+    eng.commit()
+    q = torch.randn(L, B, Hq, D, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+    torch.cuda.synchronize(device)
+    return eng, q
+
+
+def gathered_bytes(eng):
+    """Selected K+V bytes per decode layer (counts are fixed: top_k + recent per segment)."""
+    return 2 * eng.B * eng.Hkv * eng.S * eng.D * torch.empty((), dtype=eng.dtype).element_size()
+
+
+# ------------------------------------------------------------------------------------- CPU path
+def cpu_decode_sample(eng_host, wl, layers, nthreads, h2d_device=None):
+    """Runs the C restatement of the decode step on `layers` layers; returns seconds per layer
+    and a per-phase breakdown.  eng_host: list of (host_k, host_v) numpy bf16 [B,Hkv,C,D] and
+    q numpy [L,B,Hq,D]."""
+    import ctypes as C
+    from oracle import build_oracle
+    lib = build_oracle.load()
+    hk_list, hv_list, qn = eng_host
+    B, Hq, Hkv, D, T = wl["batch"], wl["q_heads"], wl["kv_heads"], wl["head_dim"], wl["seq_len"]
+    K, R = wl["top_k"], wl["recent"]
+    S = K + R
+    scores = np.empty((B * Hkv, T), dtype=np.float32)
+    idx = np.empty((B * Hkv, S), dtype=np.int32)
+    counts = np.empty(B * Hkv, dtype=np.int32)
+    out = np.empty((B, Hq, D), dtype=np.float32)
+    t = {"score": 0.0, "topk": 0.0, "gather": 0.0, "h2d": 0.0, "attention": 0.0}
+    if h2d_device is not None:
+        # the gather writes straight into pinned buffers, as index_select(out=pinned) does in
+        # the reference's get_sparse_async (kv_cache.py:594-599), then one H2D copy each
+        ks_t = torch.empty((B, Hkv, S, D), dtype=torch.int16).pin_memory()
+        vs_t = torch.empty((B, Hkv, S, D), dtype=torch.int16).pin_memory()
+        ks, vs = ks_t.numpy().view(np.uint16), vs_t.numpy().view(np.uint16)
+        dk = torch.empty(ks_t.shape, dtype=torch.int16, device=h2d_device)
+        dv = torch.empty_like(dk)
+    else:
+        ks = np.empty((B, Hkv, S, D), dtype=np.uint16)
+        vs = np.empty_like(ks)
+    for layer in layers:
+        hk, hv = hk_list[layer], hv_list[layer]
+        C_ = hk.shape[2]
+        es = 2
+        t0 = time.perf_counter()
+        lib.okv_score_bf16(qn[layer].ctypes.data, hk.ctypes.data, Hkv * C_ * D, C_ * D, D, B, Hq, Hkv, T, D,
+                           scores.ctypes.data, T, nthreads)
+        t1 = time.perf_counter()
+        lib.okv_topk(scores.ctypes.data, T, B * Hkv, Hkv, None, T, K, R, idx.ctypes.data, S, counts.ctypes.data,
+                     nthreads)
+        t2 = time.perf_counter()
+        lib.okv_gather(hk.ctypes.data, hv.ctypes.data, Hkv * C_ * D * es, C_ * D * es, D * es, B, Hkv,
+                       idx.ctypes.data, 32, Hkv * S, S, S, counts.ctypes.data, ks.ctypes.data, vs.ctypes.data,
+                       D * es, nthreads)
+        t3 = time.perf_counter()
+        if h2d_device is not None:
+            dk.copy_(ks_t, non_blocking=True)
+            dv.copy_(vs_t, non_blocking=True)
+            torch.cuda.synchronize(h2d_device)
+        t4 = time.perf_counter()
+        lib.okv_attention_bf16(qn[layer].ctypes.data, ks.ctypes.data, vs.ctypes.data, counts.ctypes.data, B, Hq,
+                               Hkv, S, D, C.c_float(1.0 / math.sqrt(D)), out.ctypes.data, nthreads)
+        t5 = time.perf_counter()
+        t["score"] += t1 - t0
+        t["topk"] += t2 - t1
+        t["gather"] += t3 - t2
+        t["h2d"] += t4 - t3
+        t["attention"] += t5 - t4
+    return sum(t.values()) / len(layers), {k: v / len(layers) * 1e3 for k, v in t.items()}
+
+
+def host_views(eng):
+    hk = [t.view(torch.int16).numpy().view(np.uint16) for t in eng.host_k]
+    hv = [t.view(torch.int16).numpy().view(np.uint16) for t in eng.host_v]
+    return hk, hv
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model():
+    try:
+        for l in open("/proc/cpuinfo"):
+            if l.startswith("model name"):
+                return l.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ------------------------------------------------------------------------------------- arms
+def run_reference(args, world, rank):
+    """The reference's CPU path (C restatement) on the host cores; rank 0 only."""
+    if rank != 0:
+        return
+    wl = dict(WORKLOAD)
+    if args.layers:
+        wl["layers"] = args.layers
+    sample_layers = min(4, wl["layers"])
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    # Host data for the sampled layers (same generator recipe as the GPU arm, on the CPU).
+    B, Hkv, D, T, Hq = wl["batch"], wl["kv_heads"], wl["head_dim"], wl["seq_len"], wl["q_heads"]
+    g = torch.Generator().manual_seed(1234)
+    n_img = int(T * wl["image_frac"])
+    hk, hv = [], []
+    for _ in range(sample_layers):
+        k = torch.randn(B, Hkv, T, D, generator=g)
+        v = torch.randn(B, Hkv, T, D, generator=g)
+        k[:, :, n_img:] *= 0.5
+        v[:, :, n_img:] *= 0.5
+        hk.append(k.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16))
+        hv.append(v.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16))
+    qn = torch.randn(sample_layers, B, Hq, D, generator=g).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    nth = cpu_threads()
+    per_layer = []
+    for step in range(args.warmup + args.steps):
+        s, _ = cpu_decode_sample((hk, hv, qn), wl, list(range(sample_layers)), nth, h2d_device=dev)
+        if step >= args.warmup:
+            per_layer.append(s)
+    sec_layer = statistics.mean(per_layer)
+    eng_bytes = 2 * B * Hkv * (wl["top_k"] + wl["recent"]) * D * 2
+    value = eng_bytes / sec_layer / 1e9
+    ms_step = sec_layer * wl["layers"] * 1e3
+    sample = (f"{sample_layers} of {wl['layers']} layers per step (same per-layer shapes), extrapolated to the "
+              f"{wl['layers']}-layer step; H2D of the gathered rows included" + ("" if dev else " (no GPU: omitted)"))
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD_NAME, "global_batch": B, "seq_len": T, "parallelism": "host cores, rank 0"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": nth, "kind": "port", "sample": sample,
+                         "cpu": cpu_model()},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_mserve(args, world, rank, local):
+    from mserve_b200 import _lib, ops
+    dev = torch.device("cuda", local)
+    wl = dict(WORKLOAD)
+    if args.layers:
+        wl["layers"] = args.layers
+    L = wl["layers"]
+    eng, q = build_engine(wl, dev, seed=1000 + rank)
+    bufs = eng.buffers()
+    peaks = pcie_peaks(dev)
+    gb_layer = gathered_bytes(eng)
+    key_bytes_layer = eng.B * eng.Hkv * wl["seq_len"] * eng.D * 2
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        for layer in range(L):
+            if ev is not None:
+                ev[layer][0].record(stream)
+            idx, cnt = eng.select(layer, q[layer], bufs)
+            if ev is not None:
+                ev[layer][1].record(stream)
+            eng.gather(layer, idx, cnt, bufs)
+            if ev is not None:
+                ev[layer][2].record(stream)
+            eng.attend(q[layer], cnt, bufs)
+            if ev is not None:
+                ev[layer][3].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    ops.check_status(dev, "bench warm-up")
+    torch.cuda.synchronize(dev)
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(L)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _lib.launch_count()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for s in range(args.steps):
+            step(evs[s])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    launches = _lib.launch_count() - launches0
+    elapsed = t0.elapsed_time(t1) * 1e-3
+    sel_ms = statistics.mean(e[l][0].elapsed_time(e[l][1]) for e in evs for l in range(L))
+    gat_ms = statistics.mean(e[l][1].elapsed_time(e[l][2]) for e in evs for l in range(L))
+    att_ms = statistics.mean(e[l][2].elapsed_time(e[l][3]) for e in evs for l in range(L))
+    ops.check_status(dev, "bench")
+    t_max = max_over_ranks(elapsed, world)
+    total_bytes = sum_over_ranks(gb_layer * L * args.steps, world)
+    value = total_bytes / t_max / 1e9
+    ms_step = t_max / args.steps * 1e3
+
+    # end to end through the public API: q from pinned host each step, outputs back to host
+    e2e = None
+    if not args.no_e2e:
+        q_host = q.cpu().pin_memory()
+        out_host = torch.empty((L,) + tuple(bufs.out.shape), dtype=bufs.out.dtype).pin_memory()
+        q_dev = torch.empty_like(q)
+        out_dev = torch.empty((L,) + tuple(bufs.out.shape), dtype=bufs.out.dtype, device=dev)
+
+        def e2e_step():
+            q_dev.copy_(q_host, non_blocking=True)
+            for layer in range(L):
+                out_dev[layer].copy_(eng.decode_layer(layer, q_dev[layer]))
+            out_host.copy_(out_dev, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        for _ in range(min(args.warmup, 3)):
+            e2e_step()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        te = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+        e2e = {"value": total_bytes / te / 1e9, "unit": "GB/s", "ms_per_step": te / args.steps * 1e3,
+               "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
+               "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+               "api": "OffloadKV.decode_layer per layer (score, top-k, gather, attention), q H2D + outputs D2H"}
+
+    # CPU baseline: the C restatement on this host's cores, rank 0 at N=1 only
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        nth = cpu_threads()
+        hk, hv = host_views(eng)
+        qn = q.cpu().view(torch.int16).numpy().view(np.uint16)
+        sample_layers = list(range(min(4, L)))
+        reps = []
+        cpu_t0 = time.perf_counter()
+        for r in range(12):          # one untimed pass, then timed passes until ~10 s of CPU work
+            s, bd = cpu_decode_sample((hk, hv, qn), wl, sample_layers, nth, h2d_device=dev)
+            if r:
+                reps.append((s, bd))
+            if r >= 2 and time.perf_counter() - cpu_t0 > 10.0:
+                break
+        s = statistics.mean(x[0] for x in reps)
+        cpu = {"value": gb_layer / s / 1e9, "unit": "GB/s", "cores": nth, "kind": "port",
+               "sample": f"layers 0-{len(sample_layers) - 1} of the same host store, {len(reps)} timed passes; per layer: "
+                         "fp32 scores, radix top-k ∪ window, index_select gather, H2D of the gathered rows, attention",
+               "ms_per_layer": s * 1e3, "breakdown_ms": reps[-1][1], "cpu": cpu_model()}
+
+    peaks_json = measured_peaks()
+    gather_gbs = gb_layer / (gat_ms * 1e-3) / 1e9
+    roofline = {"bound": "host_link", "kernel": "move_rows_kernel (mskv_gather)", "achieved": gather_gbs,
+                "peak": peaks["h2d"], "unit": "GB/s", "frac": gather_gbs / peaks["h2d"],
+                "peak_source": "pinned cudaMemcpyAsync H2D, 256 MiB, best of 5, measured in this run",
+                "algorithmic_bytes_per_launch": gb_layer, "traffic": ncu_traffic("gather")}
+    hbm_peak = peaks_json.get("hbm_gbs", 6650.0)
+    score_gbs = key_bytes_layer / (sel_ms * 1e-3) / 1e9
+    roofline_select = {"bound": "hbm", "kernel": "score_fast_kernel + topk_kernel", "achieved": score_gbs,
+                       "peak": hbm_peak, "unit": "GB/s", "frac": score_gbs / hbm_peak,
+                       "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks_json
+                       else "fallback 6650 GB/s", "algorithmic_bytes_per_launch": key_bytes_layer,
+                       "traffic": ncu_traffic("score")}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD_NAME if L == 28 else WORKLOAD_NAME + f" (layers overridden: {L})",
+                       "global_batch": wl["batch"] * world, "seq_len": wl["seq_len"],
+                       "parallelism": f"{world} rank(s), each its own 8 sequences over its own host link, "
+                                      "no collective on the data path",
+                       "l2": "inputs larger than L2: 3.76 GB of HBM keys + 1 GB of host KV read per step"},
+            "roofline": roofline, "roofline_select": roofline_select,
+            "breakdown_ms_per_layer": {"score_topk": sel_ms, "gather": gat_ms, "attention": att_ms},
+            "pcie_peak_gbs": peaks, "gather_frac_of_h2d_peak_whole_step": value / world / peaks["h2d"],
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_mserve(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,266 @@
+/*
+ * mserve_kv.h — C ABI of the B200 (sm_100a) KV-cache selection-and-offload library
+ * (libmserve_kv.so).
+ *
+ * Every entry point takes plain pointers, sizes and byte strides and a CUDA stream passed
+ * as `void*` (NULL = legacy default stream).  Nothing here allocates device memory; the
+ * caller owns every buffer.  Kernels are enqueued asynchronously on the given stream and
+ * never synchronize the device.
+ *
+ * Return value: MSKV_OK (0) or one of the MSKV_ERR_* codes; the text of the last failure on
+ * the calling thread is available from mskv_last_error().
+ *
+ * Device-side faults that depend on data (an index outside the valid token range, a page
+ * table entry that is negative) are not fatal: the offending row is skipped (a gathered row
+ * is zero-filled), and the corresponding MSKV_STATUS_* bit is OR-ed into the optional
+ * `status` word (device memory or mapped pinned host memory) so the host can raise after
+ * the stream completes.
+ *
+ * "Device-accessible" below means device memory of the current device or pinned host memory
+ * that is mapped into the device address space (cudaHostAlloc / cudaHostRegister under
+ * unified addressing).  Host KV stores are read and written in place over PCIe ("UVA",
+ * zero-copy); they are never staged through a bounce buffer.
+ *
+ * Reference interfaces replaced are cited as file:line within the MServe project
+ * (qwen-eljrte/...).
+ */
+#ifndef MSERVE_KV_H
+#define MSERVE_KV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MSKV_ABI_VERSION 1
+
+/* ---- return codes ---------------------------------------------------------------------- */
+#define MSKV_OK 0
+#define MSKV_ERR_ARG 1         /* invalid argument: null pointer, size, stride or alignment  */
+#define MSKV_ERR_NOT_MAPPED 2  /* a host pointer is not pinned + mapped for device access    */
+#define MSKV_ERR_DTYPE 3       /* unsupported element type                                    */
+#define MSKV_ERR_CUDA 4        /* CUDA runtime error (launch failure, bad device, ...)        */
+#define MSKV_ERR_RANGE 5       /* a size exceeds what the entry point supports                */
+
+/* ---- device status bits (OR-ed into the optional `status` word) ------------------------ */
+#define MSKV_STATUS_INDEX_OOB 0x1u   /* a source token index was outside [0, len)            */
+#define MSKV_STATUS_BAD_PAGE 0x2u    /* a page-table entry needed by a row was negative      */
+#define MSKV_STATUS_DST_OOB 0x4u     /* a destination token was outside [0, len)             */
+
+/* ---- element types ---------------------------------------------------------------------- */
+#define MSKV_DT_F32 0
+#define MSKV_DT_F16 1
+#define MSKV_DT_BF16 2
+#define MSKV_DT_F64 3
+#define MSKV_DT_FP8_E4M3 4
+#define MSKV_DT_FP8_E5M2 5
+
+/* ---- library ---------------------------------------------------------------------------- */
+int mskv_abi_version(void);
+const char* mskv_last_error(void);
+/* Number of kernels this library has launched in this process (all threads, all devices). */
+uint64_t mskv_launch_count(void);
+
+/* ---- pinned, mapped host memory (the offload store) --------------------------------------
+ * Replaces the `.pin_memory()` host tensors of CPUKVCache
+ * (qwen-eljrte/Qwen_Transformer/kv_cache.py:727-728, 756-759) with one allocation per layer
+ * that is pinned, mapped and portable, so every GPU of the process can read it in place.   */
+int mskv_host_alloc(void** host_ptr, uint64_t bytes);
+int mskv_host_free(void* host_ptr);
+/* Pin + map an existing host range (cudaHostRegister, mapped | portable). */
+int mskv_host_register(void* ptr, uint64_t bytes);
+int mskv_host_unregister(void* ptr);
+/* Device-accessible address of `ptr` (host-mapped or device memory).  Returns
+ * MSKV_ERR_NOT_MAPPED for pageable host memory. */
+int mskv_device_view(const void* ptr, void** dev_ptr);
+
+/* ---- (a1) UVA gather, reference layout ----------------------------------------------------
+ * Replaces uva_gather_cuda / uva_gather (qwen-eljrte/cuda_uva_kernel.cpp:48-108,
+ * qwen-eljrte/cuda_uva_kernel_v2.cpp:86-129).
+ *   k_out[b,h,s,:] = k_in[b,h,indices[s],:]   (same for v), one index list shared by all (b,h)
+ * k_in, v_in : contiguous [B,H,T,D], pinned mapped host memory (or device memory)
+ * indices    : device-accessible int64 [S]
+ * k_out,v_out: device memory, contiguous [B,H,S,D]
+ * elem_bytes : 1, 2, 4 or 8 (the copy is bit-exact for any element type of that size)
+ * Indices outside [0,T) are skipped: the output row is zero-filled and
+ * MSKV_STATUS_INDEX_OOB is set in `status` (may be NULL). */
+int mskv_uva_gather(const void* k_in, const void* v_in, const int64_t* indices,
+                    int64_t num_selected, int64_t batch_size, int64_t num_heads,
+                    int64_t seq_len, int64_t head_dim, int32_t elem_bytes,
+                    void* k_out, void* v_out, uint32_t* status, void* stream);
+
+/* ---- generic row addressing ----------------------------------------------------------------
+ * A "segment" is one (b, h) pair; a "row" is the head_dim vector of one token of one segment.
+ * The address of logical token t of segment (b, h) on one side of a move is
+ *   paged  (page_table != NULL): base + page_table[b*pt_stride_b + t/page_size]*stride_page
+ *                                     + h*stride_h + (t % page_size)*stride_t
+ *                                (a page id outside [0, num_pages) skips the row)
+ *   strided (page_table == NULL): base + b*stride_b + h*stride_h + p*stride_t,
+ *                                 p = t, or (ring_start[b] + t) mod ring_cap when ring_start
+ * and t is valid when 0 <= t < len[b] (len == NULL: len_scalar).  All strides in bytes. */
+typedef struct mskv_rows {
+  const void* base_k;
+  const void* base_v;           /* NULL: the move has no V half                       */
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_t;
+  int64_t stride_page;
+  int64_t pt_stride_b;          /* elements                                           */
+  int64_t len_scalar;
+  int64_t num_pages;            /* paged: page ids must lie in [0, num_pages)         */
+  const int32_t* page_table;
+  const int32_t* ring_start;    /* per batch; physical slot of logical token 0        */
+  const int32_t* tok0;          /* per batch; logical token of row 0 (NULL: 0)        */
+  const int32_t* len;           /* per batch; valid logical tokens (NULL: len_scalar) */
+  int32_t page_size;
+  int32_t ring_cap;
+} mskv_rows;
+
+/* ---- (a1/a2/a3) selected-row gather: per-segment indices ----------------------------------
+ * Replaces CPUKVCache.get_sparse_async_uva / get_sparse_async
+ * (qwen-eljrte/Qwen_Transformer/kv_cache.py:493-543, 545-629) and generalises the reference
+ * kernel to per-(b, KV head) index lists, ring-buffer host stores, paged sources and ragged
+ * selections.  Row s of segment (b,h) copies source token
+ *   idx[b*idx_stride_b + h*idx_stride_h + s]            (index list, int32 or int64)
+ * for s < count, count = counts ? counts[b*cnt_stride_b + h*cnt_stride_h] : num_selected,
+ * into destination token (dst.tok0 ? dst.tok0[b] : 0) + s. */
+typedef struct mskv_gather_desc {
+  mskv_rows src;
+  mskv_rows dst;
+  const void* indices;
+  int64_t idx_stride_b;         /* elements; 0 with idx_stride_h 0 = one shared list  */
+  int64_t idx_stride_h;
+  const int32_t* counts;        /* NULL: every segment has num_selected rows          */
+  int64_t cnt_stride_b;
+  int64_t cnt_stride_h;
+  int64_t row_bytes;            /* head_dim * element size                            */
+  uint32_t* status;
+  int32_t index_bits;           /* 32 or 64                                           */
+  int32_t batch;
+  int32_t heads;
+  int32_t num_selected;         /* rows per segment (upper bound when counts != NULL) */
+} mskv_gather_desc;
+int mskv_gather(const mskv_gather_desc* d, void* stream);
+
+/* ---- (c) contiguous row moves: paged append, host write-back, page write-back ------------
+ * Row i (0 <= i < n, n = counts ? counts[b] : num_tokens) of segment (b,h) copies
+ * source token (src.tok0 ? src.tok0[b] : 0) + i to destination token
+ * (dst.tok0 ? dst.tok0[b] : 0) + i.  With a paged destination this is the paged append of
+ * new KV into HBM pages; with a ring-strided host destination it is the write-back that
+ * replaces CPUKVCache.append_new's torch.cat + keep-last-max_len
+ * (qwen-eljrte/Qwen_Transformer/kv_cache.py:718-765; kv_cache_optimized.py:54-149); with a
+ * paged source and host destination it is the write-back of evicted pages. */
+typedef struct mskv_copy_desc {
+  mskv_rows src;
+  mskv_rows dst;
+  const int32_t* counts;        /* per batch; NULL: num_tokens                        */
+  int64_t row_bytes;
+  uint32_t* status;
+  int32_t batch;
+  int32_t heads;
+  int32_t num_tokens;
+  int32_t pad_;
+} mskv_copy_desc;
+int mskv_copy_rows(const mskv_copy_desc* d, void* stream);
+
+/* ---- (b) importance scores ----------------------------------------------------------------
+ * Replaces the scoring half of compute_token_importance
+ * (qwen-eljrte/Qwen_Transformer/attention.py:532-565 for "attention_score", 574 for "norm").
+ * method 0 (attention_score): scores[b,hk,t] = sum_d qsum[b,hk,d] * k[b,hk,t,d] in fp32,
+ *          qsum[b,hk,:] = sum_{g<G} q[b, hk*G+g, :]  (G = q_heads / kv_heads; the GQA group
+ *          sum, equal to the reference's per-head products summed over repeat_kv'd heads)
+ * method 1 (norm):            scores[b,hk,t] = sqrt(sum_d k[b,hk,t,d]^2) in fp32
+ * k rows are addressed by `k` (mskv_rows, base_v unused); q row (b, hq) is at
+ * q + b*q_stride_b + hq*q_stride_h (bytes); scores row (b,hk) at
+ * scores + (b*kv_heads + hk)*scores_stride (elements); tokens t >= len[b] are not written.
+ * Fast path: head_dim in {64,128,256} with 16-bit K; other shapes use a generic kernel. */
+typedef struct mskv_score_desc {
+  mskv_rows k;
+  const void* q;
+  int64_t q_stride_b;
+  int64_t q_stride_h;
+  float* scores;
+  int64_t scores_stride;
+  int64_t max_tokens;           /* upper bound of len[b] (grid size)                  */
+  int32_t dtype;                /* MSKV_DT_BF16 / F16 / F32, same for q and k         */
+  int32_t method;               /* 0 attention_score, 1 norm                          */
+  int32_t batch;
+  int32_t q_heads;
+  int32_t kv_heads;
+  int32_t head_dim;
+} mskv_score_desc;
+int mskv_score(const mskv_score_desc* d, void* stream);
+
+/* ---- (b) top-k with recent window ---------------------------------------------------------
+ * Replaces the selection half of compute_token_importance
+ * (qwen-eljrte/Qwen_Transformer/attention.py:567-572, torch.topk) and adds the recent window.
+ * Selection j (b = j / sel_per_batch) ranks the key
+ *   key(t) = scale * sum_{r<rows_per_sel} scores[(j*rows_per_sel + r)*scores_stride + t]
+ * (fp32, summed in r order) over the candidates t in [0, n), n = max(L - recent, 0),
+ * L = len[b] (NULL: len_scalar), keeps the top k = min(top_k[b] or top_k_scalar, n) by key
+ * (ties broken toward the lower token index, NaN ranks highest), and appends the window
+ * [n, L).  The output row idx[j*out_stride ...] is sorted ascending and holds
+ * count = k + (L - n) entries; counts[j] receives it (may be NULL).  Scores of the
+ * candidates only are read. */
+typedef struct mskv_topk_desc {
+  const float* scores;
+  int64_t scores_stride;
+  void* out_idx;
+  int64_t out_stride;           /* elements                                           */
+  int32_t* counts;
+  const int32_t* len;
+  const int32_t* top_k;         /* per batch, NULL: top_k_scalar                      */
+  uint32_t* status;
+  float scale;
+  int32_t len_scalar;
+  int32_t top_k_scalar;
+  int32_t recent;
+  int32_t num_sel;
+  int32_t rows_per_sel;
+  int32_t sel_per_batch;
+  int32_t out_bits;             /* 32 or 64                                           */
+} mskv_topk_desc;
+int mskv_topk(const mskv_topk_desc* d, void* stream);
+
+/* ---- sparse decode attention over the selected rows ---------------------------------------
+ * Replaces sparse_sdpa_attention (qwen-eljrte/Qwen_Transformer/attention.py:591-641):
+ *   out[b,hq,i,:] = softmax(scale * q[b,hq,i,:] . K_sel[b,hk,s,:]) V_sel[b,hk,s,:],
+ *   hk = hq / G, s < count(b,hk)
+ * in fp32, output in `dtype`.  K_sel/V_sel row s of (b,hk) at
+ *   base + (b*kv_heads + hk)*kv_stride_seg + s*kv_stride_s (bytes).
+ * q row (b,hq,i) at q + b*q_stride_b + hq*q_stride_h + i*q_stride_q (bytes), likewise out.
+ * Requires G*q_len <= 16.  `workspace` must hold mskv_attention_workspace_bytes(d) bytes of
+ * device memory (split-sequence partial results). */
+typedef struct mskv_attn_desc {
+  const void* q;
+  int64_t q_stride_b;
+  int64_t q_stride_h;
+  int64_t q_stride_q;
+  const void* k;
+  const void* v;
+  int64_t kv_stride_seg;
+  int64_t kv_stride_s;
+  const int32_t* counts;        /* per (b,hk) segment; NULL: num_selected             */
+  void* out;
+  int64_t out_stride_b;
+  int64_t out_stride_h;
+  int64_t out_stride_q;
+  void* workspace;
+  uint64_t workspace_bytes;
+  float scale;
+  int32_t dtype;                /* MSKV_DT_BF16 / F16 / F32 for q, K, V and out       */
+  int32_t batch;
+  int32_t q_heads;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t q_len;
+  int32_t num_selected;
+} mskv_attn_desc;
+uint64_t mskv_attention_workspace_bytes(const mskv_attn_desc* d);
+int mskv_sparse_attention(const mskv_attn_desc* d, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MSERVE_KV_H */

@@ -1,0 +1,144 @@
+"""Parity of scoring (mskv_score) and selection (mskv_topk) with the oracle.
+
+Scores: fp32 on the GPU vs fp64 in the oracle, within 1e-3 relative (scaled by the score
+magnitude).  Selection: bit-exact index sets when the oracle ranks the GPU's own fp32 scores;
+against the reference's golden outputs, index sets equal except at (near-)ties.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import from_bits
+from oracle import kv_oracle as ko
+
+pytestmark = pytest.mark.gpu
+
+SCORE_RTOL = 1e-3
+
+
+def _assert_scores_close(got: np.ndarray, ref: np.ndarray):
+    scale = np.abs(ref).mean() + 1e-30
+    err = np.abs(got.astype(np.float64) - ref) / (np.abs(ref) + scale)
+    assert err.max() <= SCORE_RTOL, f"max scaled error {err.max():.3e}"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("D", [64, 128, 256, 80])
+@pytest.mark.parametrize("method", ["attention_score", "norm"])
+def test_head_scores(built_lib, dtype, D, method):
+    from mserve_b200.selection import head_scores
+    g = torch.Generator().manual_seed(D)
+    B, Hq, Hkv, T = 2, 28, 4, 1000
+    q = torch.randn(B, Hq, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, T, D, generator=g).to(dtype)
+    got = head_scores(q.cuda(), k.cuda(), method).cpu().numpy()
+    ref = ko.gqa_scores(q.float().numpy(), k.float().numpy(), method=method)
+    _assert_scores_close(got, ref)
+
+
+def test_paged_scores_lens(built_lib):
+    """Keys read through a page table, per-sequence lengths, pages scattered in the pool."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(3)
+    B, Hq, Hkv, D, ps, maxp = 3, 8, 2, 128, 16, 20
+    P = B * maxp
+    pool = torch.randn(P, Hkv, ps, D, generator=g).to(torch.bfloat16)
+    perm = torch.randperm(P, generator=g).to(torch.int32).view(B, maxp)
+    lens = torch.tensor([320, 17, 200], dtype=torch.int32)
+    q = torch.randn(B, Hq, D, generator=g).to(torch.bfloat16)
+    dev = torch.device("cuda")
+    out = torch.full((B, Hkv, 320), float("nan"), device=dev)
+    rows = ops.paged_rows(pool.to(dev), None, perm.to(dev), len_=lens.to(dev))
+    ops.score(q.to(dev), rows, batch=B, kv_heads=Hkv, max_tokens=320, out=out)
+    got = out.cpu().numpy()
+    # logical K [B, Hkv, T, D] assembled on the CPU from the page table
+    kl = pool.float().numpy()[perm.numpy()]             # [B, maxp, Hkv, ps, D]
+    kl = kl.transpose(0, 2, 1, 3, 4).reshape(B, Hkv, maxp * ps, D)[:, :, :320]
+    ref = ko.gqa_scores(q.float().numpy(), kl, lens=lens.numpy())
+    for b in range(B):
+        L = int(lens[b])
+        _assert_scores_close(got[b, :, :L], ref[b, :, :L])
+        assert np.isnan(got[b, :, L:]).all()            # beyond len: untouched
+
+
+@pytest.mark.parametrize("T,K,R", [(16384, 2048, 128), (5000, 700, 0), (300, 300, 10), (300, 0, 16),
+                                   (100, 50, 200), (1, 1, 1), (4096, 4095, 0)])
+def test_topk_window_exact(built_lib, T, K, R):
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(T + K)
+    rows = torch.randn(6, T, generator=g)
+    got, cnt = ops.topk(rows.cuda(), top_k=K, recent=R)
+    ref, rcnt = ko.select_topk_window(rows.numpy(), top_k=K, recent=R)
+    got, cnt = got.cpu().numpy(), cnt.cpu().numpy()
+    np.testing.assert_array_equal(cnt, rcnt)
+    for j in range(6):
+        np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
+
+
+def test_topk_ties_nan_lens_grouped(built_lib):
+    """Heavy ties (quantised scores), NaN, -0.0/+0.0, per-sequence lengths and top_k,
+    head-summed keys with a scale (the reference's mean over heads)."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(9)
+    B, Hk, T = 3, 4, 3000
+    rows = torch.randint(-3, 4, (B * Hk, T), generator=g).float() * 0.5
+    rows[0, 5] = float("nan")
+    rows[1, :100] = -0.0
+    lens = torch.tensor([3000, 1234, 77], dtype=torch.int32)
+    topk_b = torch.tensor([500, 1000, 10], dtype=torch.int32)
+    # per-head selections
+    got, cnt = ops.topk(rows.cuda(), top_k=topk_b.cuda(), recent=32, len_=lens.cuda(), sel_per_batch=Hk)
+    ref, rcnt = ko.select_topk_window(rows.numpy(), top_k=topk_b.numpy(), recent=32, lens=lens.numpy(),
+                                      sel_per_batch=Hk)
+    got, cnt = got.cpu().numpy(), cnt.cpu().numpy()
+    np.testing.assert_array_equal(cnt, rcnt)
+    for j in range(B * Hk):
+        np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
+    # one selection per sequence over the head-summed, scaled keys
+    got, cnt = ops.topk(rows.cuda(), top_k=topk_b.cuda(), recent=0, len_=lens.cuda(), rows_per_sel=Hk,
+                        sel_per_batch=1, scale=1.0 / 28)
+    ref, rcnt = ko.select_topk_window(rows.numpy(), top_k=topk_b.numpy(), recent=0, lens=lens.numpy(),
+                                      rows_per_sel=Hk, sel_per_batch=1, scale=1.0 / 28)
+    got, cnt = got.cpu().numpy(), cnt.cpu().numpy()
+    np.testing.assert_array_equal(cnt, rcnt)
+    for j in range(B):
+        np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
+
+
+def _tie_tolerant_equal(got: np.ndarray, ref: np.ndarray, scores: np.ndarray, rtol: float):
+    """Index sets equal except for tokens whose score is within rtol of the k-th score."""
+    got_s, ref_s = set(got.tolist()), set(ref.tolist())
+    assert len(got_s) == len(got) == len(ref)
+    diff = got_s ^ ref_s
+    if not diff:
+        return
+    kth = np.sort(scores)[::-1][len(ref) - 1]
+    tol = rtol * (np.abs(scores).max() + 1e-30)
+    bad = [t for t in diff if abs(scores[t] - kth) > tol]
+    assert not bad, f"{len(bad)} indices differ away from the selection threshold"
+
+
+@pytest.mark.parametrize("case", ["cti_f64_score", "cti_f64_norm", "cti_f64_q3", "cti_f64_short", "cti_f64_b2",
+                                  "cti_f32_score", "cti_bf16_score"])
+def test_compute_token_importance_reference_golden(built_lib, golden, case):
+    """Drop-in compute_token_importance vs the reference function's own outputs."""
+    from mserve_b200.selection import compute_token_importance
+    B, Hq, Hkv, Q, T, D, method, mn = [int(x) for x in golden[f"{case}/meta"]]
+    ratio = float(golden[f"{case}/ratio"][0])
+    dt = str(golden[f"{case}/dtype"])
+    tdt = torch.bfloat16 if "bfloat16" in dt else torch.float32   # f64 inputs are scored in fp32
+    q = from_bits(golden[f"{case}/q"], torch.bfloat16 if tdt == torch.bfloat16 else torch.float64).to(tdt)
+    k = from_bits(golden[f"{case}/k"], torch.bfloat16 if tdt == torch.bfloat16 else torch.float64).to(tdt)
+    mname = ["attention_score", "norm"][method]
+    got = compute_token_importance(q.cuda(), k.cuda(), mname, ratio, mn)
+    assert got.device.type == "cpu" and got.dtype == torch.int64
+    ref = golden[f"{case}/idx"]
+    assert tuple(got.shape) == ref.shape
+    # oracle fp64 scores of the same inputs decide what counts as a near-tie
+    qn, kn = q.double().numpy(), k.double().numpy()
+    per = ko.gqa_scores(qn[:, :, -1], kn, method=mname)
+    scores = per.sum(axis=1)
+    rtol = 2e-2 if tdt == torch.bfloat16 else 1e-5
+    got2, ref2 = got.numpy().reshape(B, -1), ref.reshape(B, -1)
+    for b in range(B):
+        _tie_tolerant_equal(got2[b], ref2[b], scores[b], rtol)
