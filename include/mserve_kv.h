@@ -47,6 +47,8 @@ extern "C" {
 #define MSKV_STATUS_INDEX_OOB 0x1u   /* a source token index was outside [0, len)            */
 #define MSKV_STATUS_BAD_PAGE 0x2u    /* a page-table entry needed by a row was negative      */
 #define MSKV_STATUS_DST_OOB 0x4u     /* a destination token was outside [0, len)             */
+#define MSKV_STATUS_TIMEOUT 0x8u     /* a bounded wait on a bulk copy gave up; the kernel     */
+                                     /* skipped its remaining work                            */
 
 /* ---- element types ---------------------------------------------------------------------- */
 #define MSKV_DT_F32 0
@@ -173,8 +175,11 @@ int mskv_copy_rows(const mskv_copy_desc* d, void* stream);
  * method 1 (norm):            scores[b,hk,t] = sqrt(sum_d k[b,hk,t,d]^2) in fp32
  * k rows are addressed by `k` (mskv_rows, base_v unused); q row (b, hq) is at
  * q + b*q_stride_b + hq*q_stride_h (bytes); scores row (b,hk) at
- * scores + (b*kv_heads + hk)*scores_stride (elements); tokens t >= len[b] are not written.
- * Fast path: head_dim in {64,128,256} with 16-bit K; other shapes use a generic kernel. */
+ * scores + (b*kv_heads + hk)*scores_stride (elements); tokens t >= len[b] are not written;
+ * tokens whose page is unmapped score -inf (MSKV_STATUS_BAD_PAGE).
+ * Fast path (16-bit K, head_dim in {64,128,256}, rows contiguous, page_size dividing 128):
+ * a persistent kernel streams 128-token key tiles into shared memory with bulk copies
+ * (3-4 stages in flight); other shapes use register-streaming or generic kernels. */
 typedef struct mskv_score_desc {
   mskv_rows k;
   const void* q;
@@ -183,6 +188,7 @@ typedef struct mskv_score_desc {
   float* scores;
   int64_t scores_stride;
   int64_t max_tokens;           /* upper bound of len[b] (grid size)                  */
+  uint32_t* status;             /* optional device status word                        */
   int32_t dtype;                /* MSKV_DT_BF16 / F16 / F32, same for q and k         */
   int32_t method;               /* 0 attention_score, 1 norm                          */
   int32_t batch;
@@ -202,7 +208,9 @@ int mskv_score(const mskv_score_desc* d, void* stream);
  * (ties broken toward the lower token index, NaN ranks highest), and appends the window
  * [n, L).  The output row idx[j*out_stride ...] is sorted ascending and holds
  * count = k + (L - n) entries; counts[j] receives it (may be NULL).  Scores of the
- * candidates only are read. */
+ * candidates only are read.  When len != NULL, len_scalar must bound every len[b] (it sizes
+ * the kernel: up to 131072 candidates, a cluster of 8 CTAs per selection holds the keys in
+ * shared memory; beyond that one CTA per selection re-reads them from L2). */
 typedef struct mskv_topk_desc {
   const float* scores;
   int64_t scores_stride;
@@ -230,8 +238,10 @@ int mskv_topk(const mskv_topk_desc* d, void* stream);
  * in fp32, output in `dtype`.  K_sel/V_sel row s of (b,hk) at
  *   base + (b*kv_heads + hk)*kv_stride_seg + s*kv_stride_s (bytes).
  * q row (b,hq,i) at q + b*q_stride_b + hq*q_stride_h + i*q_stride_q (bytes), likewise out.
- * Requires G*q_len <= 16.  `workspace` must hold mskv_attention_workspace_bytes(d) bytes of
- * device memory (split-sequence partial results). */
+ * `workspace` must hold mskv_attention_workspace_bytes(d) bytes of device memory and be
+ * zero-filled before its first use: it holds the split-sequence partial results and one
+ * completion counter per segment, which every launch leaves at zero again.  Launches that
+ * share a workspace must be ordered (same stream). */
 typedef struct mskv_attn_desc {
   const void* q;
   int64_t q_stride_b;
@@ -248,6 +258,7 @@ typedef struct mskv_attn_desc {
   int64_t out_stride_q;
   void* workspace;
   uint64_t workspace_bytes;
+  uint32_t* status;             /* optional device status word                        */
   float scale;
   int32_t dtype;                /* MSKV_DT_BF16 / F16 / F32 for q, K, V and out       */
   int32_t batch;

@@ -21,6 +21,7 @@ MSKV_ERR_RANGE = 5
 STATUS_INDEX_OOB = 0x1
 STATUS_BAD_PAGE = 0x2
 STATUS_DST_OOB = 0x4
+STATUS_TIMEOUT = 0x8
 
 DT_F32 = 0
 DT_F16 = 1
@@ -66,7 +67,7 @@ class CopyDesc(C.Structure):
 class ScoreDesc(C.Structure):
     _fields_ = [
         ("k", Rows), ("q", _vp), ("q_stride_b", _i64), ("q_stride_h", _i64),
-        ("scores", _vp), ("scores_stride", _i64), ("max_tokens", _i64),
+        ("scores", _vp), ("scores_stride", _i64), ("max_tokens", _i64), ("status", _vp),
         ("dtype", _i32), ("method", _i32), ("batch", _i32), ("q_heads", _i32),
         ("kv_heads", _i32), ("head_dim", _i32),
     ]
@@ -87,7 +88,7 @@ class AttnDesc(C.Structure):
         ("k", _vp), ("v", _vp), ("kv_stride_seg", _i64), ("kv_stride_s", _i64),
         ("counts", _vp), ("out", _vp), ("out_stride_b", _i64), ("out_stride_h", _i64),
         ("out_stride_q", _i64), ("workspace", _vp), ("workspace_bytes", C.c_uint64),
-        ("scale", C.c_float), ("dtype", _i32), ("batch", _i32), ("q_heads", _i32),
+        ("status", _vp), ("scale", C.c_float), ("dtype", _i32), ("batch", _i32), ("q_heads", _i32),
         ("kv_heads", _i32), ("head_dim", _i32), ("q_len", _i32), ("num_selected", _i32),
     ]
 

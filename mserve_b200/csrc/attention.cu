@@ -5,26 +5,29 @@
 // (no repeat_kv): all G query heads (times q_len query rows) of a KV head are served by one
 // pass over that head's selected rows, so every gathered byte is read once from HBM.
 //
-// Split-sequence ("flash-decoding") schedule: CTA (segment, split) handles kTile rows.
-//   1. each 16-lane group loads 16 K rows (one 16-byte chunk per lane per row), converts
-//      once to fp32, and for every query row reduce-scatters the 16 partial dot products
-//      so lane l ends with the score of row l -> shared memory;
-//   2. per query row: tile max, exp, sum (fp32);
-//   3. V rows are streamed the same way and accumulated into per-lane fp32 accumulators,
-//      merged across groups with shared-memory atomics;
-//   4. (m, l, acc[D]) partials go to the workspace; a combine kernel merges the splits and
-//      writes the output in the input dtype.
-// Shapes outside the fast path (head_dim != 64/128, 32-bit types, > 8 query rows per KV
-// head) use a one-warp-per-output-row kernel with an online softmax.
+// Split-sequence ("flash-decoding") schedule, fast path (16-bit, D in {64,128}, G*q_len <= 8
+// or 16 for D=64, contiguous rows): CTA (segment, split) owns kTile = 64 selected rows.
+//   0. one thread starts two bulk copies (K tile, V tile: contiguous 8-16 KB each) into shared
+//      memory on an mbarrier while all threads stage their query slice in registers;
+//   1. QKᵀ: a warp serves 32/SL query rows, lane = (query row, 16-byte d-slice); each lane
+//      walks the 64 K rows (one 16-byte shared load per row, shared by the warp's query rows)
+//      accumulating one partial dot per row, then a butterfly reduce-scatter over the SL
+//      slice lanes leaves each lane with the full scores of 64/SL rows;
+//   2. tile max / exp / sum per query row with xor-shuffles; probabilities -> shared memory;
+//   3. P·V with the same lane mapping: each lane accumulates its 8 output dims directly;
+//   4. (m, l, acc) partials -> workspace; the last CTA of the segment (atomic ticket) merges
+//      the splits and writes the output, then re-arms the ticket for the next launch.
+// Other shapes use a one-warp-per-output-row kernel with an online softmax.
 #include <math.h>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace mskv {
 
-constexpr int kAtThreads = 256;
-constexpr int kTile = 256;      // rows per CTA
-constexpr int kMaxNR = 8;       // query rows per KV head on the fast path
+constexpr int kAtThreads = 128;
+constexpr int kAtTile = 64;         // selected rows per CTA
+constexpr int kAtWsHeader = 4096;   // bytes reserved for the per-segment tickets (<= 1024 segments)
 
 struct AttnDev {
   const char* q;
@@ -35,7 +38,9 @@ struct AttnDev {
   const int32_t* counts;
   char* out;
   int64_t o_sb, o_sh, o_sq;
-  float* ws;               // [seg][split][NR][D + 2]
+  unsigned* tickets;       // [segments]
+  float* ws;               // [segments][splits][nr][D + 2]
+  uint32_t* status;
   float scale;
   int32_t batch, q_heads, kv_heads, head_dim, q_len, num_sel, splits, nr, dtype;
 };
@@ -67,29 +72,38 @@ __device__ __forceinline__ void cvt8(const uint4& v, float* f, bool is_bf16) {
   }
 }
 
-template <int N>
-__device__ __forceinline__ float reduce_scatter_a(float (&v)[N], int lane) {
+// Butterfly reduce-scatter of NV values over the M lanes of a group (lane bits below M):
+// afterwards lane l holds in v[0 .. NV/M) the group sums of values [l*NV/M, (l+1)*NV/M).
+template <int NV, int M>
+__device__ __forceinline__ void reduce_scatter_n(float (&v)[NV], int lane_in_group) {
+  int c = NV;
 #pragma unroll
-  for (int o = N / 2; o >= 1; o >>= 1) {
-    const bool upper = (lane & o) != 0;
+  for (int o = M / 2; o >= 1; o >>= 1) {
+    const bool upper = (lane_in_group & o) != 0;
+    const int h = c / 2;
 #pragma unroll
-    for (int j = 0; j < o; ++j) {
-      const float send = upper ? v[j] : v[j + o];
-      const float keep = upper ? v[j + o] : v[j];
-      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    for (int j = 0; j < NV / 2; ++j) {
+      if (j < h) {
+        const float send = upper ? v[j] : v[j + h];
+        const float keep = upper ? v[j + h] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
     }
+    c = h;
   }
-  return v[0];
 }
 
-// Fast path: 16-bit types, D in {64, 128}; GL = D/8 lanes per row (8 or 16).
 template <bool BF16, int D>
-__global__ void __launch_bounds__(kAtThreads, 1) attn_partial_kernel(const AttnDev a) {
-  constexpr int GL = D / 8;                  // lanes per row == rows per group iteration
-  __shared__ float s_q[kMaxNR][D];
-  __shared__ float s_p[kMaxNR][kTile];
-  __shared__ float s_acc[kMaxNR][D];
-  __shared__ float s_m[kMaxNR], s_l[kMaxNR];
+__global__ void __launch_bounds__(kAtThreads) attn_split_kernel(const AttnDev a) {
+  constexpr int ROWB = D * 2;
+  constexpr int SL = D / 8;            // 16-byte d-slices per row = lanes per query row
+  constexpr int RPW = 32 / SL;         // query rows per warp
+  constexpr int RPL = kAtTile / SL;    // score rows per lane after the reduce-scatter
+  __shared__ __align__(128) uint8_t sK[kAtTile * ROWB];
+  __shared__ __align__(128) uint8_t sV[kAtTile * ROWB];
+  __shared__ float s_p[4 * RPW][kAtTile];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int s_last;
 
   const int seg = blockIdx.x / a.splits;
   const int split = blockIdx.x - seg * a.splits;
@@ -100,159 +114,135 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_partial_kernel(const AttnD
   int count = a.counts ? a.counts[seg] : a.num_sel;
   if (count > a.num_sel) count = a.num_sel;
   if (count < 0) count = 0;
-  const int r0 = split * kTile;
-  const int nrows = max(0, min(kTile, count - r0));
+  const int r0 = split * kAtTile;
+  const int nrows = max(0, min(kAtTile, count - r0));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int sl = lane % SL;                 // d-slice
+  const int r = warp * RPW + lane / SL;     // query row of this lane
+  const bool active = r < nr;
 
-  // Query rows of this KV head (row r = g*q_len + i) -> fp32 shared memory, pre-scaled.
-  for (int x = threadIdx.x; x < nr * D; x += kAtThreads) {
-    const int r = x / D, d = x - r * D;
-    const int g = r / a.q_len, i = r - g * a.q_len;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)(nrows * ROWB);
+    mbar_arrive_expect_tx(&bar, 2 * bytes);
+    if (bytes) {
+      bulk_load(sK, a.k + (int64_t)seg * a.kv_seg + (int64_t)r0 * a.kv_s, bytes, &bar);
+      bulk_load(sV, a.v + (int64_t)seg * a.kv_seg + (int64_t)r0 * a.kv_s, bytes, &bar);
+    }
+  }
+  // query slice of this lane (pre-scaled), while the copies are in flight
+  float qf[8];
+  {
+    const int g = active ? r / a.q_len : 0, i = active ? r - (r / a.q_len) * a.q_len : 0;
     const char* qp = a.q + (int64_t)b * a.q_sb + (int64_t)(hk * G + g) * a.q_sh + (int64_t)i * a.q_sq;
-    const float qv = BF16 ? to_f(reinterpret_cast<const __nv_bfloat16*>(qp)[d])
-                          : to_f(reinterpret_cast<const __half*>(qp)[d]);
-    s_q[r][d] = qv * a.scale;
-    s_acc[r][d] = 0.f;
+    const uint4 raw = active ? *reinterpret_cast<const uint4*>(qp + sl * 16) : make_uint4(0, 0, 0, 0);
+    cvt8(raw, qf, BF16);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qf[e] *= a.scale;
+  }
+  const bool ok = mbar_wait(&bar, 0, kWaitTimeoutNs);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0 && a.status) atomicOr(a.status, MSKV_STATUS_TIMEOUT);
+    mbar_wait(&bar, 0, kDrainTimeoutNs);
+    return;  // every CTA of the launch reaches this point together only on a broken device
+  }
+
+  // 1. scores of the 64 rows for this lane's query row (partial over its d-slice)
+  float part[kAtTile];
+#pragma unroll
+  for (int row = 0; row < kAtTile; ++row) {
+    float acc = 0.f;
+    if (row < nrows) {
+      float f[8];
+      cvt8(*reinterpret_cast<const uint4*>(sK + row * ROWB + sl * 16), f, BF16);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaf(qf[e], f[e], acc);
+    }
+    part[row] = acc;
+  }
+  reduce_scatter_n<kAtTile, SL>(part, sl);   // part[0..RPL) = rows [sl*RPL, (sl+1)*RPL)
+  // 2. softmax statistics over the tile (rows >= nrows excluded)
+  float m = -INFINITY;
+#pragma unroll
+  for (int x = 0; x < RPL; ++x)
+    if (sl * RPL + x < nrows) m = fmaxf(m, part[x]);
+#pragma unroll
+  for (int o = SL / 2; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float l = 0.f;
+#pragma unroll
+  for (int x = 0; x < RPL; ++x) {
+    const int row = sl * RPL + x;
+    const float p = row < nrows ? expf(part[x] - m) : 0.f;
+    s_p[warp * RPW + lane / SL][row] = p;
+    l += p;
+  }
+#pragma unroll
+  for (int o = SL / 2; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  __syncwarp();
+  // 3. P·V for this lane's 8 output dims
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  const float* prow = s_p[warp * RPW + lane / SL];
+  for (int row = 0; row < nrows; ++row) {
+    float f[8];
+    cvt8(*reinterpret_cast<const uint4*>(sV + row * ROWB + sl * 16), f, BF16);
+    const float p = prow[row];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = fmaf(p, f[e], acc[e]);
+  }
+  // 4. partial -> workspace, last CTA of the segment merges
+  const int64_t wstride = (int64_t)a.nr * (D + 2);
+  float* wp = a.ws + ((int64_t)seg * a.splits + split) * wstride;
+  if (active) {
+    float4* dst = reinterpret_cast<float4*>(wp + (int64_t)r * (D + 2) + sl * 8);
+    if (((uintptr_t)dst & 15) == 0) {
+      dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wp[(int64_t)r * (D + 2) + sl * 8 + e] = acc[e];
+    }
+    if (sl == 0) {
+      wp[(int64_t)r * (D + 2) + D] = nrows > 0 ? m : -INFINITY;
+      wp[(int64_t)r * (D + 2) + D + 1] = nrows > 0 ? l : 0.f;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&a.tickets[seg], 1u);
+    s_last = prev == (unsigned)(a.splits - 1);
   }
   __syncthreads();
-
-  const int tid = threadIdx.x;
-  const int gl = tid & (GL - 1);
-  const char* kseg = a.k + (int64_t)seg * a.kv_seg;
-  const char* vseg = a.v + (int64_t)seg * a.kv_seg;
-
-  // Loops run per warp (uniform trip counts, so the shuffles see all 32 lanes); the
-  // 32/GL groups of a warp take consecutive GL-row blocks of the warp's 32 rows.
-  const int warp_id = tid >> 5;
-  const int grp_in_warp = (tid & 31) / GL;
-  // 1. scores
-  for (int wb = warp_id * 32; wb < nrows; wb += kAtThreads) {
-    const int rb = wb + grp_in_warp * GL;
-    float f[GL][8];
+  if (!s_last) return;
+  __threadfence();
+  if (active) {
+    const float* base = a.ws + (int64_t)seg * a.splits * wstride + (int64_t)r * (D + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, __ldcg(base + s * wstride + D));
+    float L = 0.f, o[8];
 #pragma unroll
-    for (int j = 0; j < GL; ++j) {
-      uint4 raw = make_uint4(0, 0, 0, 0);
-      if (rb + j < nrows)
-        raw = *reinterpret_cast<const uint4*>(kseg + (int64_t)(r0 + rb + j) * a.kv_s + gl * 16);
-      cvt8(raw, f[j], BF16);
-    }
-    for (int r = 0; r < nr; ++r) {
-      float qf[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) qf[e] = s_q[r][gl * 8 + e];
-      float part[GL];
-#pragma unroll
-      for (int j = 0; j < GL; ++j) {
-        float acc = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc = fmaf(qf[e], f[j][e], acc);
-        part[j] = acc;
-      }
-      const float sc = reduce_scatter_a<GL>(part, gl);
-      if (rb + gl < nrows) s_p[r][rb + gl] = sc;
-    }
-  }
-  __syncthreads();
-
-  // 2. tile softmax statistics: warp w handles query rows w, w+8, ...
-  const int lane = tid & 31, warp = tid >> 5;
-  for (int r = warp; r < nr; r += kAtThreads / 32) {
-    float m = -INFINITY;
-    for (int x = lane; x < nrows; x += 32) m = fmaxf(m, s_p[r][x]);
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int x = lane; x < nrows; x += 32) {
-      const float p = expf(s_p[r][x] - m);
-      s_p[r][x] = p;
-      l += p;
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) { s_m[r] = m; s_l[r] = l; }
-  }
-  __syncthreads();
-
-  // 3. P·V
-  float acc[kMaxNR][8];
-#pragma unroll
-  for (int r = 0; r < kMaxNR; ++r)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
-  for (int wb = warp_id * 32; wb < nrows; wb += kAtThreads) {
-    const int rb = wb + grp_in_warp * GL;
-    uint4 raw[GL];
-#pragma unroll
-    for (int j = 0; j < GL; ++j) {
-      raw[j] = make_uint4(0, 0, 0, 0);
-      if (rb + j < nrows)
-        raw[j] = *reinterpret_cast<const uint4*>(vseg + (int64_t)(r0 + rb + j) * a.kv_s + gl * 16);
-    }
-#pragma unroll
-    for (int j = 0; j < GL; ++j) {
-      if (rb + j < nrows) {
-        float vf[8];
-        cvt8(raw[j], vf, BF16);
-#pragma unroll
-        for (int r = 0; r < kMaxNR; ++r) {
-          if (r < nr) {
-            const float p = s_p[r][rb + j];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[r][e] = fmaf(p, vf[e], acc[r][e]);
-          }
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < kMaxNR; ++r)
-    if (r < nr)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) atomicAdd(&s_acc[r][gl * 8 + e], acc[r][e]);
-  __syncthreads();
-
-  // 4. partials
-  float* wsp = a.ws + ((int64_t)seg * a.splits + split) * nr * (D + 2);
-  for (int x = tid; x < nr * D; x += kAtThreads) {
-    const int r = x / D, d = x - r * D;
-    wsp[(int64_t)r * (D + 2) + d] = s_acc[r][d];
-  }
-  if (tid < nr) {
-    wsp[(int64_t)tid * (D + 2) + D] = nrows > 0 ? s_m[tid] : -INFINITY;
-    wsp[(int64_t)tid * (D + 2) + D + 1] = nrows > 0 ? s_l[tid] : 0.f;
-  }
-}
-
-// Merges the splits of one (segment, query row) per warp and writes the output row.
-template <typename T>
-__global__ void attn_combine_kernel(const AttnDev a) {
-  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int64_t nseg = (int64_t)a.batch * a.kv_heads;
-  if (wid >= nseg * a.nr) return;
-  const int seg = (int)(wid / a.nr);
-  const int r = (int)(wid - (int64_t)seg * a.nr);
-  const int D = a.head_dim;
-  const float* base = a.ws + (int64_t)seg * a.splits * a.nr * (D + 2) + (int64_t)r * (D + 2);
-  const int64_t sstride = (int64_t)a.nr * (D + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) M = fmaxf(M, base[s * sstride + D]);
-  float L = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
-    const float m = base[s * sstride + D];
-    if (m != -INFINITY) L += base[s * sstride + D + 1] * expf(m - M);
-  }
-  const int b = seg / a.kv_heads, hk = seg - b * a.kv_heads;
-  const int G = a.q_heads / a.kv_heads;
-  const int g = r / a.q_len, i = r - g * a.q_len;
-  T* op = reinterpret_cast<T*>(a.out + (int64_t)b * a.o_sb + (int64_t)(hk * G + g) * a.o_sh + (int64_t)i * a.o_sq);
-  for (int d = lane; d < D; d += 32) {
-    float o = 0.f;
+    for (int e = 0; e < 8; ++e) o[e] = 0.f;
     for (int s = 0; s < a.splits; ++s) {
-      const float m = base[s * sstride + D];
-      if (m != -INFINITY) o += base[s * sstride + d] * expf(m - M);
+      const float ms = __ldcg(base + s * wstride + D);
+      if (ms == -INFINITY) continue;
+      const float w = expf(ms - M);
+      L += __ldcg(base + s * wstride + D + 1) * w;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] += __ldcg(base + s * wstride + sl * 8 + e) * w;
     }
-    op[d] = from_f<T>(L > 0.f ? o / L : 0.f);
+    const int g = r / a.q_len, i = r - g * a.q_len;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    T* op = reinterpret_cast<T*>(a.out + (int64_t)b * a.o_sb + (int64_t)(hk * G + g) * a.o_sh + (int64_t)i * a.o_sq);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) op[sl * 8 + e] = from_f<T>(L > 0.f ? o[e] / L : 0.f);
   }
+  if (tid == 0) a.tickets[seg] = 0u;  // re-arm for the next launch on this workspace
 }
 
 // Generic path: one warp per output row (b, hq, i); online softmax over the selected rows.
@@ -311,16 +301,6 @@ __global__ void attn_generic_kernel(const AttnDev a) {
   }
 }
 
-static bool fast_path(const mskv_attn_desc* d, int es) {
-  if (es != 2) return false;
-  if (d->head_dim != 64 && d->head_dim != 128) return false;
-  const int G = d->q_heads / d->kv_heads;
-  if (G * d->q_len > kMaxNR) return false;
-  const uint64_t al = (uint64_t)(uintptr_t)d->k | (uint64_t)(uintptr_t)d->v | (uint64_t)d->kv_stride_seg |
-                      (uint64_t)d->kv_stride_s;
-  return (al & 15) == 0;
-}
-
 static int dtype_size(int dt) {
   switch (dt) {
     case MSKV_DT_F32: return 4;
@@ -329,17 +309,33 @@ static int dtype_size(int dt) {
   }
 }
 
+static bool fast_path(const mskv_attn_desc* d) {
+  if (dtype_size(d->dtype) != 2) return false;
+  if (d->head_dim != 64 && d->head_dim != 128) return false;
+  const int G = d->q_heads / d->kv_heads;
+  const int rows_max = 4 * (32 / (d->head_dim / 8));  // 4 warps x query rows per warp
+  if (G * d->q_len > rows_max) return false;
+  if (d->kv_stride_s != (int64_t)d->head_dim * 2) return false;  // tiles are single bulk copies
+  if ((int64_t)d->batch * d->kv_heads > kAtWsHeader / 4) return false;
+  const uint64_t al = (uint64_t)(uintptr_t)d->k | (uint64_t)(uintptr_t)d->v | (uint64_t)d->kv_stride_seg |
+                      (uint64_t)(uintptr_t)d->q | (uint64_t)d->q_stride_b | (uint64_t)d->q_stride_h |
+                      (uint64_t)d->q_stride_q;
+  return (al & 15) == 0;
+}
+
+static int64_t splits_of(const mskv_attn_desc* d) {
+  return d->num_selected > 0 ? (d->num_selected + kAtTile - 1) / kAtTile : 1;
+}
+
 }  // namespace mskv
 
 using namespace mskv;
 
 extern "C" uint64_t mskv_attention_workspace_bytes(const mskv_attn_desc* d) {
   if (!d || d->kv_heads <= 0 || d->q_heads <= 0 || d->q_len <= 0 || d->batch < 0) return 0;
-  const int es = dtype_size(d->dtype);
-  if (!fast_path(d, es)) return 0;
-  const int64_t splits = d->num_selected > 0 ? (d->num_selected + kTile - 1) / kTile : 1;
+  if (!fast_path(d)) return 0;
   const int64_t nr = (int64_t)(d->q_heads / d->kv_heads) * d->q_len;
-  return (uint64_t)((int64_t)d->batch * d->kv_heads * splits * nr * (d->head_dim + 2) * 4);
+  return (uint64_t)(kAtWsHeader + (int64_t)d->batch * d->kv_heads * splits_of(d) * nr * (d->head_dim + 2) * 4);
 }
 
 extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
@@ -359,32 +355,30 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
   a.k = static_cast<const char*>(d->k); a.v = static_cast<const char*>(d->v);
   a.kv_seg = d->kv_stride_seg; a.kv_s = d->kv_stride_s; a.counts = d->counts;
   a.out = static_cast<char*>(d->out); a.o_sb = d->out_stride_b; a.o_sh = d->out_stride_h; a.o_sq = d->out_stride_q;
+  a.status = d->status;
   a.scale = d->scale; a.batch = d->batch; a.q_heads = d->q_heads; a.kv_heads = d->kv_heads;
   a.head_dim = d->head_dim; a.q_len = d->q_len; a.num_sel = d->num_selected; a.dtype = d->dtype;
   a.nr = (d->q_heads / d->kv_heads) * d->q_len;
   cudaStream_t st = as_stream(stream);
-  if (fast_path(d, es)) {
+  if (fast_path(d)) {
     const uint64_t need = mskv_attention_workspace_bytes(d);
     if (!d->workspace || d->workspace_bytes < need)
       return fail(MSKV_ERR_ARG, "mskv_sparse_attention: workspace needs %llu bytes", (unsigned long long)need);
-    a.ws = static_cast<float*>(d->workspace);
-    a.splits = d->num_selected > 0 ? (d->num_selected + kTile - 1) / kTile : 1;
+    if (((uintptr_t)d->workspace & 255) != 0) return fail(MSKV_ERR_ARG, "mskv_sparse_attention: workspace must be 256-byte aligned");
+    a.tickets = static_cast<unsigned*>(d->workspace);
+    a.ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + kAtWsHeader);
+    a.splits = (int)splits_of(d);
     const int64_t blocks = (int64_t)d->batch * d->kv_heads * a.splits;
+    if (blocks > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "mskv_sparse_attention: grid too large");
     const bool bf = d->dtype == MSKV_DT_BF16;
     if (d->head_dim == 128) {
-      if (bf) attn_partial_kernel<true, 128><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
-      else attn_partial_kernel<false, 128><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
+      if (bf) attn_split_kernel<true, 128><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
+      else attn_split_kernel<false, 128><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
     } else {
-      if (bf) attn_partial_kernel<true, 64><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
-      else attn_partial_kernel<false, 64><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
+      if (bf) attn_split_kernel<true, 64><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
+      else attn_split_kernel<false, 64><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
     }
-    int rc = after_launch("mskv_sparse_attention partial");
-    if (rc) return rc;
-    const int64_t warps = (int64_t)d->batch * d->kv_heads * a.nr;
-    const unsigned cblocks = (unsigned)((warps * 32 + 255) / 256);
-    if (bf) attn_combine_kernel<__nv_bfloat16><<<cblocks, 256, 0, st>>>(a);
-    else attn_combine_kernel<__half><<<cblocks, 256, 0, st>>>(a);
-    return after_launch("mskv_sparse_attention combine");
+    return after_launch("mskv_sparse_attention");
   }
   const int64_t rows = (int64_t)d->batch * d->q_heads * d->q_len;
   const unsigned blocks = (unsigned)((rows * 32 + 255) / 256);

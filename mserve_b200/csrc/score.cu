@@ -15,6 +15,7 @@
 //  * warps own contiguous runs of 32-row slices, so the GQA-summed query is rebuilt only when
 //    a warp crosses into a new (b, KV head) segment.
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace mskv {
 
@@ -219,6 +220,218 @@ __global__ void __launch_bounds__(256) score_generic_kernel(const ScoreDev a) {
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Bulk-copy (TMA) pipeline: the main path for 16-bit keys with contiguous rows.
+//
+// A persistent CTA of 128 threads owns a contiguous, balanced range of 128-token tiles
+// (tiles of one (b, KV head) segment are consecutive).  Warp 0 streams tiles into a ring of
+// STAGES shared-memory buffers with cp.async.bulk (paged keys: one 4 KB copy per page and
+// head, issued by one lane per page; strided keys: one copy per tile), each stage guarded by
+// an mbarrier with transaction counting.  All four warps score the resident tile: a 16-lane
+// group reads 16 rows as 16-byte chunks (256 contiguous bytes per row, conflict-free), and
+// the same butterfly reduce-scatter as above leaves each lane with one row's score.  Two
+// CTAs per SM keep up to 6 x 32 KB of key bytes in flight.
+template <int D>
+struct TmaCfg {
+  static constexpr int ROWB = D * 2;
+  static constexpr int TILE = 128;
+  static constexpr int STAGES = D == 64 ? 4 : 3;
+  static constexpr int STAGE_BYTES = TILE * ROWB;
+  static constexpr int SMEM = STAGES * STAGE_BYTES;
+};
+
+struct TmaTile {
+  int64_t seg, t0;
+  int b, h;
+  int nv;  // valid rows in the tile
+};
+
+__device__ __forceinline__ TmaTile tma_tile(const ScoreDev& a, int64_t tile, int64_t tiles_per_seg, int tile_rows) {
+  TmaTile t;
+  t.seg = tile / tiles_per_seg;
+  t.t0 = (tile - t.seg * tiles_per_seg) * tile_rows;
+  t.b = (int)(t.seg / a.kv_heads);
+  t.h = (int)(t.seg - (int64_t)t.b * a.kv_heads);
+  const int64_t L = rows_len(a.k, t.b);
+  const int64_t nv = L - t.t0;
+  t.nv = nv <= 0 ? 0 : (nv > tile_rows ? tile_rows : (int)nv);
+  return t;
+}
+
+template <typename T, int D, int METHOD, bool PAGED>
+__global__ void __launch_bounds__(128) score_tma_kernel(const ScoreDev a, uint32_t* status) {
+  using Cfg = TmaCfg<D>;
+  constexpr int EPV = 8;
+  constexpr int LPR = D / EPV;
+  constexpr int GL = LPR < 16 ? LPR : 16;
+  constexpr int VPL = LPR / GL;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[Cfg::STAGES];
+  __shared__ uint32_t s_pages_ok[Cfg::STAGES];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gl = lane & (GL - 1), grp = lane / GL;
+  const int64_t tiles_per_seg = (a.max_tokens + Cfg::TILE - 1) / Cfg::TILE;
+  const int64_t total = (int64_t)a.batch * a.kv_heads * tiles_per_seg;
+  const int64_t per = total / gridDim.x, rem = total % gridDim.x;
+  const int64_t t_begin = (int64_t)blockIdx.x * per + min((int64_t)blockIdx.x, rem);
+  const int64_t t_count = per + ((int64_t)blockIdx.x < rem ? 1 : 0);
+
+  if (tid == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // Warp 0: start the bulk copies of relative tile i into stage i % STAGES.
+  auto issue = [&](int64_t i) {
+    const TmaTile tt = tma_tile(a, t_begin + i, tiles_per_seg, Cfg::TILE);
+    const int stage = (int)(i % Cfg::STAGES);
+    uint8_t* dst = smem + stage * Cfg::STAGE_BYTES;
+    uint64_t* bar = &full[stage];
+    fence_proxy_async_smem();
+    if constexpr (PAGED) {
+      const int ps = a.k.page_size;
+      const int npages = (tt.nv + ps - 1) / ps;
+      uint32_t bytes = 0;
+      const char* src = nullptr;
+      if (lane < npages) {
+        const int64_t pidx = tt.t0 / ps + lane;
+        const int32_t page = a.k.page_table[(int64_t)tt.b * a.k.pt_stride + pidx];
+        const int rows = min(ps, tt.nv - lane * ps);
+        if (page >= 0 && page < a.k.num_pages) {
+          bytes = (uint32_t)(rows * Cfg::ROWB);
+          src = a.k.base_k + (int64_t)page * a.k.sp + (int64_t)tt.h * a.k.sh;
+        } else if (status) {
+          atomicOr(status, MSKV_STATUS_BAD_PAGE);
+        }
+      }
+      const uint32_t ok_mask = __ballot_sync(0xffffffffu, bytes > 0);
+      uint32_t sum = bytes;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) {
+        s_pages_ok[stage] = ok_mask;
+        mbar_arrive_expect_tx(bar, sum);
+      }
+      __syncwarp();
+      if (bytes) bulk_load(dst + (int64_t)lane * ps * Cfg::ROWB, src, bytes, bar);
+    } else {
+      if (lane == 0) {
+        const uint32_t bytes = (uint32_t)(tt.nv * Cfg::ROWB);
+        s_pages_ok[stage] = 0xffffffffu;
+        mbar_arrive_expect_tx(bar, bytes);
+        if (bytes)
+          bulk_load(dst, a.k.base_k + (int64_t)tt.b * a.k.sb + (int64_t)tt.h * a.k.sh + tt.t0 * a.k.st, bytes, bar);
+      }
+    }
+  };
+
+  if (warp == 0) {
+    const int64_t pre = t_count < Cfg::STAGES ? t_count : Cfg::STAGES;
+    for (int64_t i = 0; i < pre; ++i) issue(i);
+  }
+
+  float qs[VPL][EPV];
+  int64_t cur_seg = -1;
+  int64_t waited = 0;
+  bool timed_out = false;
+  for (int64_t i = 0; i < t_count; ++i) {
+    const int stage = (int)(i % Cfg::STAGES);
+    const bool ok = mbar_wait(&full[stage], (uint32_t)((i / Cfg::STAGES) & 1), kWaitTimeoutNs);
+    if (__syncthreads_or(!ok)) {
+      timed_out = true;
+      break;
+    }
+    waited = i + 1;
+    const TmaTile tt = tma_tile(a, t_begin + i, tiles_per_seg, Cfg::TILE);
+    if (tt.seg != cur_seg) {
+      cur_seg = tt.seg;
+      if constexpr (METHOD == 0) {
+        const int G = a.q_heads / a.kv_heads;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v)
+#pragma unroll
+          for (int e = 0; e < EPV; ++e) qs[v][e] = 0.f;
+        for (int g = 0; g < G; ++g) {
+          const char* qrow = a.q + (int64_t)tt.b * a.q_sb + (int64_t)(tt.h * G + g) * a.q_sh;
+#pragma unroll
+          for (int v = 0; v < VPL; ++v) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(qrow + (int64_t)(gl + v * GL) * 16);
+            float f[EPV];
+            Cvt<T>::to_f32(raw, f);
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) qs[v][e] += f[e];
+          }
+        }
+      }
+    }
+    const uint8_t* tile_smem = smem + stage * Cfg::STAGE_BYTES;
+    const uint32_t pages_ok = s_pages_ok[stage];
+#pragma unroll
+    for (int half = 0; half < Cfg::TILE / 128; ++half) {
+      const int rbase = half * 128 + warp * 32 + grp * GL;
+      float part[GL];
+#pragma unroll
+      for (int j = 0; j < GL; ++j) {
+        const int row = rbase + j;
+        float acc = 0.f;
+        if (row < tt.nv) {
+#pragma unroll
+          for (int v = 0; v < VPL; ++v) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(tile_smem + row * Cfg::ROWB + (gl + v * GL) * 16);
+            float f[EPV];
+            Cvt<T>::to_f32(raw, f);
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) {
+              if constexpr (METHOD == 0) acc = fmaf(qs[v][e], f[e], acc);
+              else acc = fmaf(f[e], f[e], acc);
+            }
+          }
+        }
+        part[j] = acc;
+      }
+      float sc = reduce_scatter<GL>(part, gl);
+      if constexpr (METHOD == 1) sc = sqrtf(sc);
+      const int row = half * 128 + warp * 32 + lane;
+      if (row < tt.nv) {
+        bool valid = true;
+        if constexpr (PAGED) valid = (pages_ok >> (row / a.k.page_size)) & 1u;
+        a.scores[tt.seg * a.scores_stride + tt.t0 + row] = valid ? sc : -INFINITY;
+      }
+    }
+    __syncthreads();  // every warp is done with this stage
+    if (warp == 0 && i + Cfg::STAGES < t_count) issue(i + Cfg::STAGES);
+  }
+  if (timed_out) {
+    if (tid == 0 && status) atomicOr(status, MSKV_STATUS_TIMEOUT);
+    // Let copies still in flight land before the CTA's shared memory is released.
+    const int64_t issued = t_count < waited + Cfg::STAGES ? t_count : waited + Cfg::STAGES;
+    for (int64_t i = waited; i < issued; ++i)
+      mbar_wait(&full[i % Cfg::STAGES], (uint32_t)((i / Cfg::STAGES) & 1), kDrainTimeoutNs);
+  }
+}
+
+template <typename T, int D, int METHOD, bool PAGED>
+static int launch_tma(ScoreDev& a, uint32_t* status, cudaStream_t st) {
+  using Cfg = TmaCfg<D>;
+  auto kern = score_tma_kernel<T, D, METHOD, PAGED>;
+  static bool attr_set = false;  // benign race: every thread sets the same value
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    attr_set = true;
+  }
+  int occ = 1;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 128, Cfg::SMEM);
+  if (occ < 1) occ = 1;
+  const int64_t tiles = (int64_t)a.batch * a.kv_heads * ((a.max_tokens + Cfg::TILE - 1) / Cfg::TILE);
+  int64_t grid = (int64_t)num_sms() * occ;
+  if (grid > tiles) grid = tiles;
+  if (grid < 1) grid = 1;
+  kern<<<(unsigned)grid, 128, Cfg::SMEM, st>>>(a, status);
+  return after_launch("mskv_score");
+}
+
 template <typename T, int D, int METHOD, bool PAGED>
 static int launch_fast(ScoreDev& a, cudaStream_t st) {
   auto kern = score_fast_kernel<T, D, METHOD, PAGED>;
@@ -237,7 +450,18 @@ static int launch_fast(ScoreDev& a, cudaStream_t st) {
 }
 
 template <typename T, int METHOD>
-static int dispatch_d(ScoreDev& a, bool paged, bool fast, cudaStream_t st) {
+static int dispatch_d(ScoreDev& a, bool paged, bool fast, bool tma, uint32_t* status, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    if (tma) {
+#define MSKV_TMA_CASE(DD)                                                              \
+  if (a.head_dim == DD) return paged ? launch_tma<T, DD, METHOD, true>(a, status, st)  \
+                                     : launch_tma<T, DD, METHOD, false>(a, status, st);
+      MSKV_TMA_CASE(64)
+      MSKV_TMA_CASE(128)
+      MSKV_TMA_CASE(256)
+#undef MSKV_TMA_CASE
+    }
+  }
   if (fast) {
 #define MSKV_SCORE_CASE(DD)                                                      \
   if (a.head_dim == DD) return paged ? launch_fast<T, DD, METHOD, true>(a, st)   \
@@ -263,8 +487,9 @@ static int dispatch_d(ScoreDev& a, bool paged, bool fast, cudaStream_t st) {
 }
 
 template <typename T>
-static int dispatch_method(ScoreDev& a, bool paged, bool fast, cudaStream_t st) {
-  return a.method == 0 ? dispatch_d<T, 0>(a, paged, fast, st) : dispatch_d<T, 1>(a, paged, fast, st);
+static int dispatch_method(ScoreDev& a, bool paged, bool fast, bool tma, uint32_t* status, cudaStream_t st) {
+  return a.method == 0 ? dispatch_d<T, 0>(a, paged, fast, tma, status, st)
+                       : dispatch_d<T, 1>(a, paged, fast, tma, status, st);
 }
 
 }  // namespace mskv
@@ -309,10 +534,15 @@ extern "C" int mskv_score(const mskv_score_desc* d, void* stream) {
     const int gl = lpr < 16 ? lpr : 16;
     fast = fast && gl > 0 && (d->k.page_size % gl) == 0;
   }
+  // The bulk-copy pipeline also needs contiguous rows (a tile or page is one copy) and, when
+  // paged, pages of 4..128 tokens that tile the 128-token key tiles exactly.
+  bool tma = fast && es == 2 && d->k.stride_t == (int64_t)d->head_dim * es &&
+             (d->head_dim == 64 || d->head_dim == 128 || d->head_dim == 256);
+  if (paged) tma = tma && d->k.page_size >= 4 && d->k.page_size <= 128 && (128 % d->k.page_size) == 0;
   cudaStream_t st = as_stream(stream);
   switch (d->dtype) {
-    case MSKV_DT_F32: return dispatch_method<float>(a, paged, fast, st);
-    case MSKV_DT_F16: return dispatch_method<__half>(a, paged, fast, st);
-    default: return dispatch_method<__nv_bfloat16>(a, paged, fast, st);
+    case MSKV_DT_F32: return dispatch_method<float>(a, paged, fast, false, d->status, st);
+    case MSKV_DT_F16: return dispatch_method<__half>(a, paged, fast, tma, d->status, st);
+    default: return dispatch_method<__nv_bfloat16>(a, paged, fast, tma, d->status, st);
   }
 }

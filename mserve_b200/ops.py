@@ -302,6 +302,7 @@ def score(q: torch.Tensor, k: RowsSpec, *, batch: int, kv_heads: int, max_tokens
     d.scores = out.data_ptr()
     d.scores_stride = out.stride(1)
     d.max_tokens = max_tokens
+    d.status = status_word(out.device).data_ptr()
     d.dtype = _DTYPE_CODE[k.dtype]
     d.method = method
     d.batch, d.q_heads, d.kv_heads, d.head_dim = batch, Hq, kv_heads, D
@@ -374,7 +375,9 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     key = (device.index, torch.cuda.current_stream(device).cuda_stream)
     w = _workspaces.get(key)
     if w is None or w.numel() < nbytes:
-        w = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        # zero-filled: the attention workspace starts with per-segment tickets that every
+        # launch leaves at zero
+        w = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
         _workspaces[key] = w
     return w
 
@@ -418,6 +421,7 @@ def sparse_attention(q: torch.Tensor, k_sel: torch.Tensor, v_sel: torch.Tensor, 
     d.out = out.data_ptr()
     d.out_stride_b, d.out_stride_h, d.out_stride_q = out.stride(0) * es, out.stride(1) * es, out.stride(2) * es
     d.scale = float(scale if scale is not None else 1.0 / math.sqrt(D))
+    d.status = status_word(q.device).data_ptr()
     d.dtype = _DTYPE_CODE[q.dtype]
     d.batch, d.q_heads, d.kv_heads, d.head_dim, d.q_len, d.num_selected = B, Hq, Hk, D, Q, S
     need = int(lib().mskv_attention_workspace_bytes(C.byref(d)))

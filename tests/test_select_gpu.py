@@ -142,3 +142,30 @@ def test_compute_token_importance_reference_golden(built_lib, golden, case):
     got2, ref2 = got.numpy().reshape(B, -1), ref.reshape(B, -1)
     for b in range(B):
         _tie_tolerant_equal(got2[b], ref2[b], scores[b], rtol)
+
+
+def test_topk_beyond_cluster_capacity(built_lib):
+    """More than 8 x 16384 candidates: the single-CTA path re-reading scores from L2."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(21)
+    rows = torch.randn(3, 140000, generator=g)
+    got, cnt = ops.topk(rows.cuda(), top_k=9000, recent=64)
+    ref, rcnt = ko.select_topk_window(rows.numpy(), top_k=9000, recent=64)
+    got, cnt = got.cpu().numpy(), cnt.cpu().numpy()
+    np.testing.assert_array_equal(cnt, rcnt)
+    for j in range(3):
+        np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
+
+
+def test_scores_strided_rows(built_lib):
+    """Keys with a token stride of two rows (register-streaming path) and a capacity view."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(6)
+    B, Hq, Hkv, T, D = 2, 8, 2, 600, 128
+    big = torch.randn(B, Hkv, 2 * T, D, generator=g).to(torch.bfloat16).cuda()
+    q = torch.randn(B, Hq, D, generator=g).to(torch.bfloat16)
+    for k in (big[:, :, ::2, :], big[:, :, :T, :]):
+        out = torch.empty(B, Hkv, T, device="cuda")
+        ops.score(q.cuda(), ops.strided_rows(k, None), batch=B, kv_heads=Hkv, max_tokens=T, out=out)
+        ref = ko.gqa_scores(q.float().numpy(), k.float().cpu().numpy())
+        _assert_scores_close(out.cpu().numpy(), ref)
