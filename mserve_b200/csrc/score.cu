@@ -3,8 +3,11 @@
 // The reference computes torch.matmul(q, Kᵀ) over repeat_kv'd heads and averages over all
 // query heads (qwen-eljrte/Qwen_Transformer/attention.py:558-565).  Here the GQA group is
 // folded first: sum_g q_g·k = (sum_g q_g)·k, so every K element is read once from HBM and
-// costs one FMA.  The kernel is a memory-bound GEMV (tensor cores are deliberately unused):
+// costs one FMA.  The kernels are memory-bound GEMVs (tensor cores are deliberately unused).
+// 16-bit keys with head_dim 64/128/256 take score_stream_kernel (below); fp32 keys take
+// score_fast_kernel; any other shape the generic one-warp-per-row kernel.
 //
+// score_fast_kernel:
 //  * a group of GL lanes (GL = 16 for bf16 D=128) owns GL consecutive rows per iteration;
 //    lane l loads the l-th 16-byte chunk of each of those rows (GL independent 16-byte loads
 //    in flight per lane, 256 contiguous bytes per row per instruction), converts to fp32 and
@@ -14,8 +17,9 @@
 //    32 scores as one coalesced 128-byte store;
 //  * warps own contiguous runs of 32-row slices, so the GQA-summed query is rebuilt only when
 //    a warp crosses into a new (b, KV head) segment.
+#include <type_traits>
+
 #include "common.cuh"
-#include "tma.cuh"
 
 namespace mskv {
 
@@ -185,6 +189,167 @@ __global__ void __launch_bounds__(256) score_fast_kernel(const ScoreDev a) {
   }
 }
 
+// Main path for 16-bit keys: register streaming, 8 rows per lane group.
+//
+// GL = D/8 lanes own one row (one 16-byte chunk each); a group of GL lanes takes 8
+// consecutive rows per iteration, so every lane keeps exactly 8 independent 16-byte loads in
+// flight (ld.global.nc with L1 bypass and a 256-byte L2 prefetch: one bf16 row) and the
+// kernel stays at <= 64 registers, i.e. 32+ resident warps per SM and ~128 KB of key bytes in
+// flight per SM.  Products use packed fp32x2 FMAs (two lanes of fp32 per instruction); the
+// 8 partial dots are reduce-scattered over 8 lanes and finished with xor-shuffles.
+// (A shared-memory bulk-copy pipeline was measured slower: shared memory caps it at ~8
+// resident warps per SM, too few to hide the per-row arithmetic latency.)
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void ffma2(float2& acc, const float2 a, const float2 b) {
+  uint64_t c, x, y;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(acc.x), "f"(acc.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b.x), "f"(b.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(acc.x), "=f"(acc.y) : "l"(c));
+}
+
+template <typename T>
+__device__ __forceinline__ float2 pair_f32(uint32_t w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  } else {
+    __half2 h;
+    memcpy(&h, &w, 4);
+    return __half22float2(h);
+  }
+}
+
+template <int NV, int M>
+__device__ __forceinline__ void reduce_scatter_n(float (&v)[NV], int lane_in_group) {
+  int c = NV;
+#pragma unroll
+  for (int o = M / 2; o >= 1; o >>= 1) {
+    const bool upper = (lane_in_group & o) != 0;
+    const int h = c / 2;
+#pragma unroll
+    for (int j = 0; j < NV / 2; ++j) {
+      if (j < h) {
+        const float send = upper ? v[j] : v[j + h];
+        const float keep = upper ? v[j + h] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    c = h;
+  }
+}
+
+template <typename T, int D, int METHOD, bool PAGED>
+__global__ void __launch_bounds__(256) score_stream_kernel(const ScoreDev a) {
+  constexpr int GL = D / 8;          // lanes per row
+  constexpr int RPG = 8;             // rows per group iteration
+  constexpr int GPW = 32 / GL;       // groups per warp
+  constexpr int RPW = RPG * GPW;     // rows per warp iteration
+  static_assert(GL >= 8 && GL <= 32, "head_dim must be 64, 128 or 256");
+
+  const int lane = threadIdx.x & 31;
+  const int gl = lane % GL, grp = lane / GL;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t s_begin = warp * a.slices_per_warp;
+  const int64_t s_end = min(s_begin + a.slices_per_warp, a.total_slices);
+
+  float2 qs[4];
+  int64_t cur_seg = -1;
+  int b = 0, h = 0;
+  int64_t len = 0;
+  for (int64_t s = s_begin; s < s_end; ++s) {
+    const int64_t seg = s / a.slices_per_seg;
+    const int64_t t_slice = (s - seg * a.slices_per_seg) * RPW;
+    if (seg != cur_seg) {
+      cur_seg = seg;
+      b = (int)(seg / a.kv_heads);
+      h = (int)(seg - (int64_t)b * a.kv_heads);
+      len = rows_len(a.k, b);
+      if constexpr (METHOD == 0) {
+        const int G = a.q_heads / a.kv_heads;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) qs[i] = make_float2(0.f, 0.f);
+        for (int g = 0; g < G; ++g) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_sb +
+                                                            (int64_t)(h * G + g) * a.q_sh + gl * 16);
+          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = pair_f32<T>(w[i]);
+            qs[i].x += f.x;
+            qs[i].y += f.y;
+          }
+        }
+      }
+    }
+    if (t_slice >= len) continue;  // warp-uniform
+    const int64_t t0 = t_slice + grp * RPG;
+    bool ok = t0 < len;
+    int64_t off0 = 0;
+    if (ok) {
+      if constexpr (PAGED) {
+        const int64_t pidx = t0 / a.k.page_size;
+        const int32_t page = a.k.page_table[(int64_t)b * a.k.pt_stride + pidx];
+        ok = page >= 0 && page < a.k.num_pages;
+        off0 = (int64_t)page * a.k.sp + (int64_t)h * a.k.sh + (t0 - pidx * a.k.page_size) * a.k.st;
+      } else {
+        off0 = (int64_t)b * a.k.sb + (int64_t)h * a.k.sh + t0 * a.k.st;
+      }
+    }
+    uint4 raw[RPG];
+#pragma unroll
+    for (int j = 0; j < RPG; ++j) {
+      raw[j] = make_uint4(0, 0, 0, 0);
+      if (ok && t0 + j < len) raw[j] = ldg_stream(a.k.base_k + off0 + (int64_t)j * a.k.st + gl * 16);
+    }
+    float part[RPG];
+#pragma unroll
+    for (int j = 0; j < RPG; ++j) {
+      const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = pair_f32<T>(w[i]);
+        if constexpr (METHOD == 0) ffma2(acc, qs[i], f);
+        else ffma2(acc, f, f);
+      }
+      part[j] = acc.x + acc.y;
+    }
+    reduce_scatter_n<RPG, 8>(part, gl & 7);
+    float sc = part[0];
+#pragma unroll
+    for (int o = 8; o < GL; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+    if constexpr (METHOD == 1) sc = sqrtf(sc);
+    const int64_t t = t0 + (gl & 7);
+    if (gl < 8 && t < len) a.scores[seg * a.scores_stride + t] = ok ? sc : -INFINITY;
+  }
+}
+
+template <typename T, int D, int METHOD, bool PAGED>
+static int launch_stream(ScoreDev& a, cudaStream_t st) {
+  constexpr int RPW = 8 * (32 / (D / 8));
+  auto kern = score_stream_kernel<T, D, METHOD, PAGED>;
+  int occ = 1;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, 0);
+  if (occ < 1) occ = 1;
+  a.slices_per_seg = (a.max_tokens + RPW - 1) / RPW;
+  a.total_slices = (int64_t)a.batch * a.kv_heads * a.slices_per_seg;
+  int64_t warps = (int64_t)num_sms() * occ * 8;
+  if (warps > a.total_slices) warps = a.total_slices;
+  a.slices_per_warp = (a.total_slices + warps - 1) / warps;
+  const int64_t used_warps = (a.total_slices + a.slices_per_warp - 1) / a.slices_per_warp;
+  const int blocks = (int)((used_warps + 7) / 8);
+  kern<<<blocks, 256, 0, st>>>(a);
+  return after_launch("mskv_score");
+}
+
 // Generic path: any head_dim, element-wise loads, one warp per row.
 template <typename T, int METHOD>
 __global__ void __launch_bounds__(256) score_generic_kernel(const ScoreDev a) {
@@ -220,218 +385,6 @@ __global__ void __launch_bounds__(256) score_generic_kernel(const ScoreDev a) {
   }
 }
 
-// ---------------------------------------------------------------------------------------
-// Bulk-copy (TMA) pipeline: the main path for 16-bit keys with contiguous rows.
-//
-// A persistent CTA of 128 threads owns a contiguous, balanced range of 128-token tiles
-// (tiles of one (b, KV head) segment are consecutive).  Warp 0 streams tiles into a ring of
-// STAGES shared-memory buffers with cp.async.bulk (paged keys: one 4 KB copy per page and
-// head, issued by one lane per page; strided keys: one copy per tile), each stage guarded by
-// an mbarrier with transaction counting.  All four warps score the resident tile: a 16-lane
-// group reads 16 rows as 16-byte chunks (256 contiguous bytes per row, conflict-free), and
-// the same butterfly reduce-scatter as above leaves each lane with one row's score.  Two
-// CTAs per SM keep up to 6 x 32 KB of key bytes in flight.
-template <int D>
-struct TmaCfg {
-  static constexpr int ROWB = D * 2;
-  static constexpr int TILE = 128;
-  static constexpr int STAGES = D == 64 ? 4 : 3;
-  static constexpr int STAGE_BYTES = TILE * ROWB;
-  static constexpr int SMEM = STAGES * STAGE_BYTES;
-};
-
-struct TmaTile {
-  int64_t seg, t0;
-  int b, h;
-  int nv;  // valid rows in the tile
-};
-
-__device__ __forceinline__ TmaTile tma_tile(const ScoreDev& a, int64_t tile, int64_t tiles_per_seg, int tile_rows) {
-  TmaTile t;
-  t.seg = tile / tiles_per_seg;
-  t.t0 = (tile - t.seg * tiles_per_seg) * tile_rows;
-  t.b = (int)(t.seg / a.kv_heads);
-  t.h = (int)(t.seg - (int64_t)t.b * a.kv_heads);
-  const int64_t L = rows_len(a.k, t.b);
-  const int64_t nv = L - t.t0;
-  t.nv = nv <= 0 ? 0 : (nv > tile_rows ? tile_rows : (int)nv);
-  return t;
-}
-
-template <typename T, int D, int METHOD, bool PAGED>
-__global__ void __launch_bounds__(128) score_tma_kernel(const ScoreDev a, uint32_t* status) {
-  using Cfg = TmaCfg<D>;
-  constexpr int EPV = 8;
-  constexpr int LPR = D / EPV;
-  constexpr int GL = LPR < 16 ? LPR : 16;
-  constexpr int VPL = LPR / GL;
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full[Cfg::STAGES];
-  __shared__ uint32_t s_pages_ok[Cfg::STAGES];
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gl = lane & (GL - 1), grp = lane / GL;
-  const int64_t tiles_per_seg = (a.max_tokens + Cfg::TILE - 1) / Cfg::TILE;
-  const int64_t total = (int64_t)a.batch * a.kv_heads * tiles_per_seg;
-  const int64_t per = total / gridDim.x, rem = total % gridDim.x;
-  const int64_t t_begin = (int64_t)blockIdx.x * per + min((int64_t)blockIdx.x, rem);
-  const int64_t t_count = per + ((int64_t)blockIdx.x < rem ? 1 : 0);
-
-  if (tid == 0) {
-    for (int s = 0; s < Cfg::STAGES; ++s) mbar_init(&full[s], 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  // Warp 0: start the bulk copies of relative tile i into stage i % STAGES.
-  auto issue = [&](int64_t i) {
-    const TmaTile tt = tma_tile(a, t_begin + i, tiles_per_seg, Cfg::TILE);
-    const int stage = (int)(i % Cfg::STAGES);
-    uint8_t* dst = smem + stage * Cfg::STAGE_BYTES;
-    uint64_t* bar = &full[stage];
-    fence_proxy_async_smem();
-    if constexpr (PAGED) {
-      const int ps = a.k.page_size;
-      const int npages = (tt.nv + ps - 1) / ps;
-      uint32_t bytes = 0;
-      const char* src = nullptr;
-      if (lane < npages) {
-        const int64_t pidx = tt.t0 / ps + lane;
-        const int32_t page = a.k.page_table[(int64_t)tt.b * a.k.pt_stride + pidx];
-        const int rows = min(ps, tt.nv - lane * ps);
-        if (page >= 0 && page < a.k.num_pages) {
-          bytes = (uint32_t)(rows * Cfg::ROWB);
-          src = a.k.base_k + (int64_t)page * a.k.sp + (int64_t)tt.h * a.k.sh;
-        } else if (status) {
-          atomicOr(status, MSKV_STATUS_BAD_PAGE);
-        }
-      }
-      const uint32_t ok_mask = __ballot_sync(0xffffffffu, bytes > 0);
-      uint32_t sum = bytes;
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) {
-        s_pages_ok[stage] = ok_mask;
-        mbar_arrive_expect_tx(bar, sum);
-      }
-      __syncwarp();
-      if (bytes) bulk_load(dst + (int64_t)lane * ps * Cfg::ROWB, src, bytes, bar);
-    } else {
-      if (lane == 0) {
-        const uint32_t bytes = (uint32_t)(tt.nv * Cfg::ROWB);
-        s_pages_ok[stage] = 0xffffffffu;
-        mbar_arrive_expect_tx(bar, bytes);
-        if (bytes)
-          bulk_load(dst, a.k.base_k + (int64_t)tt.b * a.k.sb + (int64_t)tt.h * a.k.sh + tt.t0 * a.k.st, bytes, bar);
-      }
-    }
-  };
-
-  if (warp == 0) {
-    const int64_t pre = t_count < Cfg::STAGES ? t_count : Cfg::STAGES;
-    for (int64_t i = 0; i < pre; ++i) issue(i);
-  }
-
-  float qs[VPL][EPV];
-  int64_t cur_seg = -1;
-  int64_t waited = 0;
-  bool timed_out = false;
-  for (int64_t i = 0; i < t_count; ++i) {
-    const int stage = (int)(i % Cfg::STAGES);
-    const bool ok = mbar_wait(&full[stage], (uint32_t)((i / Cfg::STAGES) & 1), kWaitTimeoutNs);
-    if (__syncthreads_or(!ok)) {
-      timed_out = true;
-      break;
-    }
-    waited = i + 1;
-    const TmaTile tt = tma_tile(a, t_begin + i, tiles_per_seg, Cfg::TILE);
-    if (tt.seg != cur_seg) {
-      cur_seg = tt.seg;
-      if constexpr (METHOD == 0) {
-        const int G = a.q_heads / a.kv_heads;
-#pragma unroll
-        for (int v = 0; v < VPL; ++v)
-#pragma unroll
-          for (int e = 0; e < EPV; ++e) qs[v][e] = 0.f;
-        for (int g = 0; g < G; ++g) {
-          const char* qrow = a.q + (int64_t)tt.b * a.q_sb + (int64_t)(tt.h * G + g) * a.q_sh;
-#pragma unroll
-          for (int v = 0; v < VPL; ++v) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(qrow + (int64_t)(gl + v * GL) * 16);
-            float f[EPV];
-            Cvt<T>::to_f32(raw, f);
-#pragma unroll
-            for (int e = 0; e < EPV; ++e) qs[v][e] += f[e];
-          }
-        }
-      }
-    }
-    const uint8_t* tile_smem = smem + stage * Cfg::STAGE_BYTES;
-    const uint32_t pages_ok = s_pages_ok[stage];
-#pragma unroll
-    for (int half = 0; half < Cfg::TILE / 128; ++half) {
-      const int rbase = half * 128 + warp * 32 + grp * GL;
-      float part[GL];
-#pragma unroll
-      for (int j = 0; j < GL; ++j) {
-        const int row = rbase + j;
-        float acc = 0.f;
-        if (row < tt.nv) {
-#pragma unroll
-          for (int v = 0; v < VPL; ++v) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(tile_smem + row * Cfg::ROWB + (gl + v * GL) * 16);
-            float f[EPV];
-            Cvt<T>::to_f32(raw, f);
-#pragma unroll
-            for (int e = 0; e < EPV; ++e) {
-              if constexpr (METHOD == 0) acc = fmaf(qs[v][e], f[e], acc);
-              else acc = fmaf(f[e], f[e], acc);
-            }
-          }
-        }
-        part[j] = acc;
-      }
-      float sc = reduce_scatter<GL>(part, gl);
-      if constexpr (METHOD == 1) sc = sqrtf(sc);
-      const int row = half * 128 + warp * 32 + lane;
-      if (row < tt.nv) {
-        bool valid = true;
-        if constexpr (PAGED) valid = (pages_ok >> (row / a.k.page_size)) & 1u;
-        a.scores[tt.seg * a.scores_stride + tt.t0 + row] = valid ? sc : -INFINITY;
-      }
-    }
-    __syncthreads();  // every warp is done with this stage
-    if (warp == 0 && i + Cfg::STAGES < t_count) issue(i + Cfg::STAGES);
-  }
-  if (timed_out) {
-    if (tid == 0 && status) atomicOr(status, MSKV_STATUS_TIMEOUT);
-    // Let copies still in flight land before the CTA's shared memory is released.
-    const int64_t issued = t_count < waited + Cfg::STAGES ? t_count : waited + Cfg::STAGES;
-    for (int64_t i = waited; i < issued; ++i)
-      mbar_wait(&full[i % Cfg::STAGES], (uint32_t)((i / Cfg::STAGES) & 1), kDrainTimeoutNs);
-  }
-}
-
-template <typename T, int D, int METHOD, bool PAGED>
-static int launch_tma(ScoreDev& a, uint32_t* status, cudaStream_t st) {
-  using Cfg = TmaCfg<D>;
-  auto kern = score_tma_kernel<T, D, METHOD, PAGED>;
-  static bool attr_set = false;  // benign race: every thread sets the same value
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    attr_set = true;
-  }
-  int occ = 1;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 128, Cfg::SMEM);
-  if (occ < 1) occ = 1;
-  const int64_t tiles = (int64_t)a.batch * a.kv_heads * ((a.max_tokens + Cfg::TILE - 1) / Cfg::TILE);
-  int64_t grid = (int64_t)num_sms() * occ;
-  if (grid > tiles) grid = tiles;
-  if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, 128, Cfg::SMEM, st>>>(a, status);
-  return after_launch("mskv_score");
-}
-
 template <typename T, int D, int METHOD, bool PAGED>
 static int launch_fast(ScoreDev& a, cudaStream_t st) {
   auto kern = score_fast_kernel<T, D, METHOD, PAGED>;
@@ -450,16 +403,12 @@ static int launch_fast(ScoreDev& a, cudaStream_t st) {
 }
 
 template <typename T, int METHOD>
-static int dispatch_d(ScoreDev& a, bool paged, bool fast, bool tma, uint32_t* status, cudaStream_t st) {
+static int dispatch_d(ScoreDev& a, bool paged, bool fast, bool stream16, cudaStream_t st) {
   if constexpr (sizeof(T) == 2) {
-    if (tma) {
-#define MSKV_TMA_CASE(DD)                                                              \
-  if (a.head_dim == DD) return paged ? launch_tma<T, DD, METHOD, true>(a, status, st)  \
-                                     : launch_tma<T, DD, METHOD, false>(a, status, st);
-      MSKV_TMA_CASE(64)
-      MSKV_TMA_CASE(128)
-      MSKV_TMA_CASE(256)
-#undef MSKV_TMA_CASE
+    if (stream16) {
+      if (a.head_dim == 64) return paged ? launch_stream<T, 64, METHOD, true>(a, st) : launch_stream<T, 64, METHOD, false>(a, st);
+      if (a.head_dim == 128) return paged ? launch_stream<T, 128, METHOD, true>(a, st) : launch_stream<T, 128, METHOD, false>(a, st);
+      if (a.head_dim == 256) return paged ? launch_stream<T, 256, METHOD, true>(a, st) : launch_stream<T, 256, METHOD, false>(a, st);
     }
   }
   if (fast) {
@@ -487,9 +436,8 @@ static int dispatch_d(ScoreDev& a, bool paged, bool fast, bool tma, uint32_t* st
 }
 
 template <typename T>
-static int dispatch_method(ScoreDev& a, bool paged, bool fast, bool tma, uint32_t* status, cudaStream_t st) {
-  return a.method == 0 ? dispatch_d<T, 0>(a, paged, fast, tma, status, st)
-                       : dispatch_d<T, 1>(a, paged, fast, tma, status, st);
+static int dispatch_method(ScoreDev& a, bool paged, bool fast, bool stream16, cudaStream_t st) {
+  return a.method == 0 ? dispatch_d<T, 0>(a, paged, fast, stream16, st) : dispatch_d<T, 1>(a, paged, fast, stream16, st);
 }
 
 }  // namespace mskv
@@ -534,15 +482,14 @@ extern "C" int mskv_score(const mskv_score_desc* d, void* stream) {
     const int gl = lpr < 16 ? lpr : 16;
     fast = fast && gl > 0 && (d->k.page_size % gl) == 0;
   }
-  // The bulk-copy pipeline also needs contiguous rows (a tile or page is one copy) and, when
-  // paged, pages of 4..128 tokens that tile the 128-token key tiles exactly.
-  bool tma = fast && es == 2 && d->k.stride_t == (int64_t)d->head_dim * es &&
-             (d->head_dim == 64 || d->head_dim == 128 || d->head_dim == 256);
-  if (paged) tma = tma && d->k.page_size >= 4 && d->k.page_size <= 128 && (128 % d->k.page_size) == 0;
+  // The 16-bit streaming path needs head_dim 64/128/256 and, when paged, pages holding whole
+  // 8-row groups.
+  bool stream16 = fast && es == 2 && (d->head_dim == 64 || d->head_dim == 128 || d->head_dim == 256);
+  if (paged) stream16 = stream16 && (d->k.page_size % 8) == 0;
   cudaStream_t st = as_stream(stream);
   switch (d->dtype) {
-    case MSKV_DT_F32: return dispatch_method<float>(a, paged, fast, false, d->status, st);
-    case MSKV_DT_F16: return dispatch_method<__half>(a, paged, fast, tma, d->status, st);
-    default: return dispatch_method<__nv_bfloat16>(a, paged, fast, tma, d->status, st);
+    case MSKV_DT_F32: return dispatch_method<float>(a, paged, fast, false, st);
+    case MSKV_DT_F16: return dispatch_method<__half>(a, paged, fast, stream16, st);
+    default: return dispatch_method<__nv_bfloat16>(a, paged, fast, stream16, st);
   }
 }

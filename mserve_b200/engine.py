@@ -180,6 +180,98 @@ class OffloadKV:
         self.gather(layer, idx, counts, bufs)
         return self.attend(q, counts, bufs)
 
+    # ------------------------------------------------------------------ pipelined decode step
+    def _chunk_ops(self, layer: int, q: torch.Tensor, b0: int, b1: int, bufs: DecodeBuffers, T: int):
+        """Kernels of one layer for sequences [b0, b1): (select, gather, attend) closures."""
+        Hkv, C = self.Hkv, self.C
+        nb = b1 - b0
+        lens = self.lens[b0:b1]
+        scores = bufs.scores[b0:b1]
+        idx = bufs.idx[b0 * Hkv:b1 * Hkv]
+        counts = bufs.counts[b0 * Hkv:b1 * Hkv]
+        k_sel, v_sel = bufs.k_sel[b0:b1], bufs.v_sel[b0:b1]
+
+        def select():
+            keys = ops.paged_rows(self.pool_k[layer], None, self.page_table[b0:b1], len_=lens)
+            ops.score(q[b0:b1], keys, batch=nb, kv_heads=Hkv, max_tokens=T, out=scores, method=0)
+            ops.topk(scores.view(nb * Hkv, C), top_k=self.top_k, recent=self.recent, len_=lens, len_scalar=T,
+                     rows_per_sel=1, sel_per_batch=Hkv, out=idx, counts=counts)
+
+        def gather():
+            src = ops.strided_rows(self.host_k[layer][b0:b1], self.host_v[layer][b0:b1], len_=lens,
+                                   ring_start=self.ring_start[b0:b1], ring_cap=C, device=self.device)
+            ops.gather(src, idx.view(nb, Hkv, -1), k_sel, v_sel, batch=nb, counts=counts.view(nb, Hkv))
+
+        def attend(out):
+            ops.sparse_attention(q[b0:b1].unsqueeze(2), k_sel, v_sel, counts=counts.view(nb, Hkv), out=out[b0:b1])
+
+        return select, gather, attend
+
+    def decode_step(self, q_all: torch.Tensor, out_all: torch.Tensor, chunks: int = 4, streams=None) -> None:
+        """All layers of one decode step, pipelined over sequence chunks.
+
+        q_all: [L, B, Hq, D]; out_all: [L, B, Hq, 1, D].  Within a layer, chunk c's scores and
+        selection run on the caller's stream, its gather on a second stream and its attention
+        on a third, so the selection of chunk c+1 and the attention of chunk c-1 execute while
+        chunk c's rows cross PCIe.  Layer l+1 starts only after layer l's attention (the model
+        dependency).  The side streams fork from and join back into the caller's stream, so
+        the call can be captured in a CUDA graph.  Outputs are bit-identical to decode_layer.
+        """
+        bufs = self.buffers()
+        T = int(self.len_h.max(initial=0))
+        cur = torch.cuda.current_stream(self.device)
+        s_gat, s_att = streams or self._side_streams()
+        bounds = np.linspace(0, self.B, min(chunks, self.B) + 1).astype(int)
+        start = torch.cuda.Event()
+        start.record(cur)
+        s_gat.wait_event(start)
+        s_att.wait_event(start)
+        for layer in range(self.L):
+            sel_ev, gat_ev = [], []
+            parts = [self._chunk_ops(layer, q_all[layer], int(bounds[c]), int(bounds[c + 1]), bufs, T)
+                     for c in range(len(bounds) - 1)]
+            for select, _, _ in parts:
+                select()
+                e = torch.cuda.Event()
+                e.record(cur)
+                sel_ev.append(e)
+            with torch.cuda.stream(s_gat):
+                for (_, gather, _), e in zip(parts, sel_ev):
+                    s_gat.wait_event(e)
+                    gather()
+                    g = torch.cuda.Event()
+                    g.record(s_gat)
+                    gat_ev.append(g)
+            with torch.cuda.stream(s_att):
+                for (_, _, attend), g in zip(parts, gat_ev):
+                    s_att.wait_event(g)
+                    attend(out_all[layer])
+                done = torch.cuda.Event()
+                done.record(s_att)
+            cur.wait_event(done)                # the next layer's query needs this layer's output
+        end = torch.cuda.Event()
+        end.record(s_gat)
+        cur.wait_event(end)
+
+    def _side_streams(self):
+        if getattr(self, "_streams", None) is None:
+            self._streams = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+        return self._streams
+
+    def capture_decode_step(self, q_all: torch.Tensor, out_all: torch.Tensor, chunks: int = 4):
+        """CUDA graph of ``decode_step`` on fixed q/out buffers; returns the graph (``.replay()``).
+
+        Replaying the graph launches every kernel of the step at once.  The buffers and the
+        engine must stay alive, and the cache must not grow, while the graph is in use.
+        """
+        side = self._side_streams()
+        self.decode_step(q_all, out_all, chunks, side)      # warm-up: allocates workspaces
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, capture_error_mode="relaxed"):
+            self.decode_step(q_all, out_all, chunks, side)
+        return g
+
     # ------------------------------------------------------------------ views for tests / baselines
     def host_logical(self, layer: int, b: int):
         """Logical-order host K/V of sequence b (CPU tensors [Hkv, len, D])."""
