@@ -271,6 +271,23 @@ typedef struct mskv_attn_desc {
 uint64_t mskv_attention_workspace_bytes(const mskv_attn_desc* d);
 int mskv_sparse_attention(const mskv_attn_desc* d, void* stream);
 
+/* ---- sparse decode attention without any allocation -----------------------------------------
+ * No counterpart in the reference: an addition for callers that cannot allocate device memory
+ * where they run attention (code under an allocator lock or inside another library's memory
+ * pool, host frameworks that forbid cudaMalloc on the decode path, callers with no allocator
+ * to hand out a workspace).  Same computation and arguments as mskv_sparse_attention, but
+ * d->workspace / d->workspace_bytes are ignored: the workspace is a device array of
+ * MSKV_NOALLOC_ATTN_SCRATCH_BYTES built into the library, which each GPU that loads the
+ * library holds until the process exits.  Shapes whose mskv_attention_workspace_bytes()
+ * exceeds that size are rejected with MSKV_ERR_RANGE.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture.  Every call on a device shares the array (its
+ * completion counters are cleared by each call), so calls that overlap on the GPU -- on
+ * streams not ordered with each other -- race and give wrong results.  Calls no cudaMalloc
+ * or cudaFree. */
+#define MSKV_NOALLOC_ATTN_SCRATCH_BYTES (8u << 20)
+int mskv_sparse_attention_noalloc(const mskv_attn_desc* d, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,6 +20,8 @@
 // Other shapes use a one-warp-per-output-row kernel with an online softmax.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "tma.cuh"
 
@@ -388,4 +390,63 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
     default: attn_generic_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a); break;
   }
   return after_launch("mskv_sparse_attention");
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant of mskv_sparse_attention.
+//
+// Some callers cannot allocate device memory at the point where they run attention: code
+// that runs under an allocator lock or inside another library's memory pool, plugins whose
+// host framework forbids cudaMalloc on its hot path, or callers that have no allocator of
+// their own to hand out a workspace.  For them the split-sequence workspace lives in one
+// file-scope device array of MSKV_NOALLOC_ATTN_SCRATCH_BYTES, which every GPU that loads
+// this library keeps until the process exits.  Its device address is looked up once per
+// device (cudaGetSymbolAddress, on that device's first call) and cached; nothing is
+// allocated or freed.  All calls on a device share the array, so calls that overlap on the
+// GPU (different streams without ordering) race on it.
+static __device__ __align__(256) unsigned char g_attn_scratch[MSKV_NOALLOC_ATTN_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_dev[kMaxDevices] = {};
+
+int scratch_of_current_device(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(MSKV_ERR_RANGE, "device index %d beyond %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_dev[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(attention scratch)");
+    g_scratch_dev[dev] = p;
+  }
+  *out = g_scratch_dev[dev];
+  return MSKV_OK;
+}
+}  // namespace
+
+extern "C" int mskv_sparse_attention_noalloc(const mskv_attn_desc* d, void* stream) {
+  if (!d) return fail(MSKV_ERR_ARG, "mskv_sparse_attention_noalloc: NULL descriptor");
+  const uint64_t need = mskv_attention_workspace_bytes(d);
+  if (need > (uint64_t)MSKV_NOALLOC_ATTN_SCRATCH_BYTES)
+    return fail(MSKV_ERR_RANGE,
+                "mskv_sparse_attention_noalloc: this shape needs %llu bytes of scratch, more than the built-in "
+                "%llu; use mskv_sparse_attention with a caller-provided workspace",
+                (unsigned long long)need, (unsigned long long)MSKV_NOALLOC_ATTN_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  int rc = scratch_of_current_device(&scratch);
+  if (rc != MSKV_OK) return rc;
+  mskv_attn_desc c = *d;
+  c.workspace = scratch;
+  c.workspace_bytes = MSKV_NOALLOC_ATTN_SCRATCH_BYTES;
+  if (need > 0) {
+    // The per-segment tickets must start at zero; the array keeps whatever the last call
+    // (possibly an interrupted one) left there.
+    cudaError_t e = cudaMemsetAsync(scratch, 0, kAtWsHeader, as_stream(stream));
+    if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(attention scratch tickets)");
+  }
+  return mskv_sparse_attention(&c, stream);
 }
