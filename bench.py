@@ -467,7 +467,7 @@ def run_mserve(args, world, rank, local):
                 "algorithmic_bytes_per_launch": gb_layer, "traffic": ncu_traffic("gather")}
     hbm_peak = peaks_json.get("hbm_gbs", 6650.0)
     score_gbs = key_bytes_layer / (sel_ms * 1e-3) / 1e9
-    roofline_select = {"bound": "hbm", "kernel": "score_fast_kernel + topk_kernel", "achieved": score_gbs,
+    roofline_select = {"bound": "hbm", "kernel": "score_stream_kernel + topk_cluster_kernel", "achieved": score_gbs,
                        "peak": hbm_peak, "unit": "GB/s", "frac": score_gbs / hbm_peak,
                        "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks_json
                        else "fallback 6650 GB/s", "algorithmic_bytes_per_launch": key_bytes_layer,

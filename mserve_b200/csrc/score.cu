@@ -208,12 +208,7 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 }
 
 __device__ __forceinline__ void ffma2(float2& acc, const float2 a, const float2 b) {
-  uint64_t c, x, y;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(acc.x), "f"(acc.y));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a.x), "f"(a.y));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b.x), "f"(b.y));
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(x), "l"(y));
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(acc.x), "=f"(acc.y) : "l"(c));
+  acc = __ffma2_rn(a, b, acc);  // one packed fp32x2 FMA (sm_100)
 }
 
 template <typename T>
@@ -246,89 +241,146 @@ __device__ __forceinline__ void reduce_scatter_n(float (&v)[NV], int lane_in_gro
   }
 }
 
-template <typename T, int D, int METHOD, bool PAGED>
-__global__ void __launch_bounds__(256) score_stream_kernel(const ScoreDev a) {
-  constexpr int GL = D / 8;          // lanes per row
-  constexpr int RPG = 8;             // rows per group iteration
-  constexpr int GPW = 32 / GL;       // groups per warp
-  constexpr int RPW = RPG * GPW;     // rows per warp iteration
-  static_assert(GL >= 8 && GL <= 32, "head_dim must be 64, 128 or 256");
+// One 8-row group of a 16/32/8-row slice: where its rows are and whether they exist.
+struct SliceRef {
+  int64_t seg, t0, len, off0;
+  int b, h;
+  bool live;  // the slice starts before the segment's end (warp-uniform)
+  bool ok;    // this lane group has rows and their page is mapped
+};
 
+template <int D, bool PAGED>
+__device__ __forceinline__ SliceRef locate_slice(const ScoreDev& a, int64_t seg, int64_t slice_in_seg, int grp) {
+  constexpr int RPW = 8 * (32 / (D / 8));
+  SliceRef r;
+  r.seg = seg;
+  r.b = (int)(seg / a.kv_heads);
+  r.h = (int)(seg - (int64_t)r.b * a.kv_heads);
+  r.len = rows_len(a.k, r.b);
+  const int64_t t_slice = slice_in_seg * RPW;
+  r.live = t_slice < r.len;
+  r.t0 = t_slice + grp * 8;
+  r.ok = r.t0 < r.len;
+  r.off0 = 0;
+  if (r.ok) {
+    if constexpr (PAGED) {
+      const int64_t pidx = r.t0 / a.k.page_size;
+      const int32_t page = a.k.page_table[(int64_t)r.b * a.k.pt_stride + pidx];
+      r.ok = page >= 0 && page < a.k.num_pages;
+      r.off0 = (int64_t)page * a.k.sp + (int64_t)r.h * a.k.sh + (r.t0 - pidx * a.k.page_size) * a.k.st;
+    } else {
+      r.off0 = (int64_t)r.b * a.k.sb + (int64_t)r.h * a.k.sh + r.t0 * a.k.st;
+    }
+  }
+  return r;
+}
+
+__device__ __forceinline__ void issue_rows(const ScoreDev& a, const SliceRef& r, int gl, uint4 (&raw)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    raw[j] = make_uint4(0, 0, 0, 0);
+    if (r.ok && r.t0 + j < r.len) raw[j] = ldg_stream(a.k.base_k + r.off0 + (int64_t)j * a.k.st + gl * 16);
+  }
+}
+
+template <typename T, int D, int METHOD>
+__device__ __forceinline__ void score_rows(const ScoreDev& a, const SliceRef& r, int gl, const float2 (&qs)[4],
+                                           const uint4 (&raw)[8]) {
+  constexpr int GL = D / 8;
+  float part[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = pair_f32<T>(w[i]);
+      if constexpr (METHOD == 0) ffma2(acc, qs[i], f);
+      else ffma2(acc, f, f);
+    }
+    part[j] = acc.x + acc.y;
+  }
+  reduce_scatter_n<8, 8>(part, gl & 7);
+  float sc = part[0];
+#pragma unroll
+  for (int o = 8; o < GL; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+  if constexpr (METHOD == 1) sc = sqrtf(sc);
+  const int64_t t = r.t0 + (gl & 7);
+  if (gl < 8 && t < r.len) a.scores[r.seg * a.scores_stride + t] = r.ok ? sc : -INFINITY;
+}
+
+template <typename T>
+__device__ __forceinline__ void gqa_query(const ScoreDev& a, int b, int h, int gl, float2 (&qs)[4]) {
+  const int G = a.q_heads / a.kv_heads;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qs[i] = make_float2(0.f, 0.f);
+  for (int g = 0; g < G; ++g) {
+    const uint4 raw =
+        *reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_sb + (int64_t)(h * G + g) * a.q_sh + gl * 16);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = pair_f32<T>(w[i]);
+      qs[i].x += f.x;
+      qs[i].y += f.y;
+    }
+  }
+}
+
+// Each warp walks its contiguous run of slices with two register buffers: the 8 loads of
+// slice s+1 are issued before slice s is scored, so every lane always has 8 loads in flight.
+template <typename T, int D, int METHOD, bool PAGED>
+__global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) {
+  constexpr int GL = D / 8;
+  static_assert(GL >= 8 && GL <= 32, "head_dim must be 64, 128 or 256");
   const int lane = threadIdx.x & 31;
   const int gl = lane % GL, grp = lane / GL;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t s_begin = warp * a.slices_per_warp;
   const int64_t s_end = min(s_begin + a.slices_per_warp, a.total_slices);
+  if (s_begin >= s_end) return;
 
+  int64_t seg = s_begin / a.slices_per_seg;
+  int64_t sis = s_begin - seg * a.slices_per_seg;
+  auto advance = [&]() {
+    if (++sis == a.slices_per_seg) {
+      sis = 0;
+      ++seg;
+    }
+  };
   float2 qs[4];
-  int64_t cur_seg = -1;
-  int b = 0, h = 0;
-  int64_t len = 0;
-  for (int64_t s = s_begin; s < s_end; ++s) {
-    const int64_t seg = s / a.slices_per_seg;
-    const int64_t t_slice = (s - seg * a.slices_per_seg) * RPW;
-    if (seg != cur_seg) {
-      cur_seg = seg;
-      b = (int)(seg / a.kv_heads);
-      h = (int)(seg - (int64_t)b * a.kv_heads);
-      len = rows_len(a.k, b);
-      if constexpr (METHOD == 0) {
-        const int G = a.q_heads / a.kv_heads;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) qs[i] = make_float2(0.f, 0.f);
-        for (int g = 0; g < G; ++g) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_sb +
-                                                            (int64_t)(h * G + g) * a.q_sh + gl * 16);
-          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = pair_f32<T>(w[i]);
-            qs[i].x += f.x;
-            qs[i].y += f.y;
-          }
-        }
+  int64_t q_seg = -1;
+  auto score = [&](const SliceRef& r, const uint4 (&raw)[8]) {
+    if (!r.live) return;  // warp-uniform
+    if constexpr (METHOD == 0) {
+      if (r.seg != q_seg) {
+        q_seg = r.seg;
+        gqa_query<T>(a, r.b, r.h, gl, qs);
       }
     }
-    if (t_slice >= len) continue;  // warp-uniform
-    const int64_t t0 = t_slice + grp * RPG;
-    bool ok = t0 < len;
-    int64_t off0 = 0;
-    if (ok) {
-      if constexpr (PAGED) {
-        const int64_t pidx = t0 / a.k.page_size;
-        const int32_t page = a.k.page_table[(int64_t)b * a.k.pt_stride + pidx];
-        ok = page >= 0 && page < a.k.num_pages;
-        off0 = (int64_t)page * a.k.sp + (int64_t)h * a.k.sh + (t0 - pidx * a.k.page_size) * a.k.st;
-      } else {
-        off0 = (int64_t)b * a.k.sb + (int64_t)h * a.k.sh + t0 * a.k.st;
-      }
+    score_rows<T, D, METHOD>(a, r, gl, qs, raw);
+  };
+
+  uint4 bufA[8], bufB[8];
+  SliceRef cur = locate_slice<D, PAGED>(a, seg, sis, grp);
+  issue_rows(a, cur, gl, bufA);
+  for (int64_t s = s_begin; s < s_end; s += 2) {
+    SliceRef nxt;
+    const bool has1 = s + 1 < s_end;
+    if (has1) {
+      advance();
+      nxt = locate_slice<D, PAGED>(a, seg, sis, grp);
+      issue_rows(a, nxt, gl, bufB);
     }
-    uint4 raw[RPG];
-#pragma unroll
-    for (int j = 0; j < RPG; ++j) {
-      raw[j] = make_uint4(0, 0, 0, 0);
-      if (ok && t0 + j < len) raw[j] = ldg_stream(a.k.base_k + off0 + (int64_t)j * a.k.st + gl * 16);
+    score(cur, bufA);
+    if (!has1) break;
+    const bool has2 = s + 2 < s_end;
+    if (has2) {
+      advance();
+      cur = locate_slice<D, PAGED>(a, seg, sis, grp);
+      issue_rows(a, cur, gl, bufA);
     }
-    float part[RPG];
-#pragma unroll
-    for (int j = 0; j < RPG; ++j) {
-      const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
-      float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = pair_f32<T>(w[i]);
-        if constexpr (METHOD == 0) ffma2(acc, qs[i], f);
-        else ffma2(acc, f, f);
-      }
-      part[j] = acc.x + acc.y;
-    }
-    reduce_scatter_n<RPG, 8>(part, gl & 7);
-    float sc = part[0];
-#pragma unroll
-    for (int o = 8; o < GL; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-    if constexpr (METHOD == 1) sc = sqrtf(sc);
-    const int64_t t = t0 + (gl & 7);
-    if (gl < 8 && t < len) a.scores[seg * a.scores_stride + t] = ok ? sc : -INFINITY;
+    score(nxt, bufB);
   }
 }
 
