@@ -47,8 +47,8 @@ extern "C" {
 #define MSKV_STATUS_INDEX_OOB 0x1u   /* a source token index was outside [0, len)            */
 #define MSKV_STATUS_BAD_PAGE 0x2u    /* a page-table entry needed by a row was negative      */
 #define MSKV_STATUS_DST_OOB 0x4u     /* a destination token was outside [0, len)             */
-#define MSKV_STATUS_TIMEOUT 0x8u     /* a bounded wait on a bulk copy gave up; the kernel     */
-                                     /* skipped its remaining work                            */
+#define MSKV_STATUS_TIMEOUT 0x8u     /* reserved for kernels with bounded waits (none wait at */
+                                     /* present: every kernel here runs without spin-waits)   */
 
 /* ---- element types ---------------------------------------------------------------------- */
 #define MSKV_DT_F32 0
@@ -238,10 +238,9 @@ int mskv_topk(const mskv_topk_desc* d, void* stream);
  * in fp32, output in `dtype`.  K_sel/V_sel row s of (b,hk) at
  *   base + (b*kv_heads + hk)*kv_stride_seg + s*kv_stride_s (bytes).
  * q row (b,hq,i) at q + b*q_stride_b + hq*q_stride_h + i*q_stride_q (bytes), likewise out.
- * `workspace` must hold mskv_attention_workspace_bytes(d) bytes of device memory and be
- * zero-filled before its first use: it holds the split-sequence partial results and one
- * completion counter per segment, which every launch leaves at zero again.  Launches that
- * share a workspace must be ordered (same stream). */
+ * `workspace` must hold mskv_attention_workspace_bytes(d) bytes of device memory (the
+ * split-sequence partial results; every launch writes all it reads, so no initialisation is
+ * needed).  Launches that share a workspace must be ordered (same stream). */
 typedef struct mskv_attn_desc {
   const void* q;
   int64_t q_stride_b;
@@ -281,10 +280,10 @@ int mskv_sparse_attention(const mskv_attn_desc* d, void* stream);
  * library holds until the process exits.  Shapes whose mskv_attention_workspace_bytes()
  * exceeds that size are rejected with MSKV_ERR_RANGE.  The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress) with that device current; make that
- * first call before any stream capture.  Every call on a device shares the array (its
- * completion counters are cleared by each call), so calls that overlap on the GPU -- on
- * streams not ordered with each other -- race and give wrong results.  Calls no cudaMalloc
- * or cudaFree. */
+ * first call before any stream capture.  Every call on a device shares the array and
+ * rewrites every part of it that it reads, so calls that overlap on the GPU -- on streams
+ * not ordered with each other -- race and give wrong results.  Calls no cudaMalloc or
+ * cudaFree. */
 #define MSKV_NOALLOC_ATTN_SCRATCH_BYTES (8u << 20)
 int mskv_sparse_attention_noalloc(const mskv_attn_desc* d, void* stream);
 

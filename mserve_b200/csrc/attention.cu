@@ -5,31 +5,28 @@
 // (no repeat_kv): all G query heads (times q_len query rows) of a KV head are served by one
 // pass over that head's selected rows, so every gathered byte is read once from HBM.
 //
-// Split-sequence ("flash-decoding") schedule, fast path (16-bit, D in {64,128}, G*q_len <= 8
-// or 16 for D=64, contiguous rows): CTA (segment, split) owns kTile = 64 selected rows.
-//   0. one thread starts two bulk copies (K tile, V tile: contiguous 8-16 KB each) into shared
-//      memory on an mbarrier while all threads stage their query slice in registers;
-//   1. QKᵀ: a warp serves 32/SL query rows, lane = (query row, 16-byte d-slice); each lane
-//      walks the 64 K rows (one 16-byte shared load per row, shared by the warp's query rows)
-//      accumulating one partial dot per row, then a butterfly reduce-scatter over the SL
-//      slice lanes leaves each lane with the full scores of 64/SL rows;
-//   2. tile max / exp / sum per query row with xor-shuffles; probabilities -> shared memory;
-//   3. P·V with the same lane mapping: each lane accumulates its 8 output dims directly;
-//   4. (m, l, acc) partials -> workspace; the last CTA of the segment (atomic ticket) merges
-//      the splits and writes the output, then re-arms the ticket for the next launch.
+// Split-sequence ("flash-decoding") schedule on the tensor cores, fast path (16-bit, D in
+// {64,128}, G*q_len <= 16, 16-byte aligned rows): CTA (segment, split) owns kAtTile = 128
+// selected rows, 32 per warp; see attn_mma_kernel.  The splits' (m, l, O) partials are merged
+// by a second kernel, one block per (segment, query row).
 // Other shapes use a one-warp-per-output-row kernel with an online softmax.
 #include <math.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
-#include "tma.cuh"
+
+namespace mskv {
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+}  // namespace mskv
 
 namespace mskv {
 
 constexpr int kAtThreads = 128;
-constexpr int kAtTile = 64;         // selected rows per CTA
-constexpr int kAtWsHeader = 4096;   // bytes reserved for the per-segment tickets (<= 1024 segments)
+constexpr int kAtTile = 128;        // selected rows per CTA (32 per warp)
 
 struct AttnDev {
   const char* q;
@@ -40,7 +37,6 @@ struct AttnDev {
   const int32_t* counts;
   char* out;
   int64_t o_sb, o_sh, o_sq;
-  unsigned* tickets;       // [segments]
   float* ws;               // [segments][splits][nr][D + 2]
   uint32_t* status;
   float scale;
@@ -95,17 +91,67 @@ __device__ __forceinline__ void reduce_scatter_n(float (&v)[NV], int lane_in_gro
   }
 }
 
+// ---- tensor-core fragments (mma.sync m16n8k16, fp32 accumulate) -----------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (BF16) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+}
+
+// Fast path: the query rows of one KV head (G*q_len <= 16, padded to the MMA's 16 rows) against
+// a tile of kAtTile selected rows.  Warp w owns rows [32w, 32w+32) of the tile:
+//   * its K and V rows arrive as 16-byte cp.async chunks into shared memory with a padded row
+//     stride (ROWB + 16 bytes, so ldmatrix reads are bank-conflict free);
+//   * S = Q·Kᵀ: 4 n-tiles x D/16 k-steps of mma.m16n8k16 (K rows are the col-major B operand,
+//     ldmatrix without transpose), fp32 accumulate; scale, mask rows beyond the count, row
+//     max/sum across the four lanes that share a query row;
+//   * O = P·V: P is re-packed from the S accumulators into A fragments (bf16/fp16), V comes
+//     in through ldmatrix.trans; D/8 n-tiles x 2 k-steps;
+//   * the four warps' (m, l, O) are merged in shared memory into the CTA's split partial in
+//     the workspace; attn_merge_kernel then merges the splits and writes the output.
+// The MMAs do not speed up a memory-bound step; they remove the per-element fp32 conversions
+// and FMAs that made a CUDA-core version instruction bound.
 template <bool BF16, int D>
-__global__ void __launch_bounds__(kAtThreads) attn_split_kernel(const AttnDev a) {
+__global__ void __launch_bounds__(kAtThreads) attn_mma_kernel(const AttnDev a) {
   constexpr int ROWB = D * 2;
-  constexpr int SL = D / 8;            // 16-byte d-slices per row = lanes per query row
-  constexpr int RPW = 32 / SL;         // query rows per warp
-  constexpr int RPL = kAtTile / SL;    // score rows per lane after the reduce-scatter
-  __shared__ __align__(128) uint8_t sK[kAtTile * ROWB];
-  __shared__ __align__(128) uint8_t sV[kAtTile * ROWB];
-  __shared__ float s_p[4 * RPW][kAtTile];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ int s_last;
+  constexpr int ROWP = ROWB + 16;       // padded shared-memory row stride (bytes)
+  constexpr int KS = D / 16;            // k-steps of Q·Kᵀ
+  constexpr int NT = D / 8;             // n-tiles of P·V
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sK = smem;                                   // [kAtTile][ROWP]
+  uint8_t* sV = smem + kAtTile * ROWP;                  // [kAtTile][ROWP]
+  uint8_t* sQ = smem + 2 * kAtTile * ROWP;              // [16][ROWP]
+  __shared__ float s_m[4][16], s_l[4][16];
 
   const int seg = blockIdx.x / a.splits;
   const int split = blockIdx.x - seg * a.splits;
@@ -119,132 +165,202 @@ __global__ void __launch_bounds__(kAtThreads) attn_split_kernel(const AttnDev a)
   const int r0 = split * kAtTile;
   const int nrows = max(0, min(kAtTile, count - r0));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int sl = lane % SL;                 // d-slice
-  const int r = warp * RPW + lane / SL;     // query row of this lane
-  const bool active = r < nr;
+  const int g = lane >> 2, tig = lane & 3;
+  const int wrow0 = warp * 32;                          // first tile row of this warp
+  const int wrows = max(0, min(32, nrows - wrow0));     // this warp's valid rows
 
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_barrier_init();
+  // query rows (zero beyond nr), 16-byte chunks
+  for (int x = tid; x < 16 * (ROWB / 16); x += kAtThreads) {
+    const int r = x / (ROWB / 16), c = x - r * (ROWB / 16);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nr) {
+      const int gq = r / a.q_len, i = r - gq * a.q_len;
+      v = *reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_sb + (int64_t)(hk * G + gq) * a.q_sh +
+                                          (int64_t)i * a.q_sq + c * 16);
+    }
+    *reinterpret_cast<uint4*>(sQ + r * ROWP + c * 16) = v;
+  }
+  // this warp's K/V rows: 16-byte cp.async chunks into the padded layout (a warp moves two
+  // contiguous 256-byte rows per instruction); rows past the count are zero-filled so the
+  // masked (P = 0) columns of P·V multiply finite values
+  {
+    constexpr int CPR = ROWB / 16;                       // chunks per row
+    const char* kbase = a.k + (int64_t)seg * a.kv_seg + (int64_t)(r0 + wrow0) * a.kv_s;
+    const char* vbase = a.v + (int64_t)seg * a.kv_seg + (int64_t)(r0 + wrow0) * a.kv_s;
+    for (int x = lane; x < 32 * CPR; x += 32) {
+      const int r = x / CPR, c = x - r * CPR;
+      uint8_t* dk = sK + (wrow0 + r) * ROWP + c * 16;
+      uint8_t* dv = sV + (wrow0 + r) * ROWP + c * 16;
+      if (r < wrows) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dk)),
+                     "l"(kbase + (int64_t)r * a.kv_s + c * 16) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dv)),
+                     "l"(vbase + (int64_t)r * a.kv_s + c * 16) : "memory");
+      } else {
+        *reinterpret_cast<uint4*>(dk) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(dv) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  __syncthreads();  // query rows visible to every warp
+  // Q fragments for all k-steps (rows 0..15)
+  uint32_t qa[KS][4];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk) {
+    const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int col = kk * 16 + 8 * (lane >> 4);
+    ldsm_x4(qa[kk], sQ + row * ROWP + col * 2);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncwarp();     // the warp's own rows (copied and zero-filled by its lanes) are visible
+
+  // S = Q·Kᵀ for the warp's 32 rows: n-tile j covers rows wrow0 + 8j .. +7
+  float sacc[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sacc[j][e] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int kk = 0; kk < KS; kk += 2) {
+      uint32_t kb[4];
+      const int row = wrow0 + 8 * j + (lane & 7);
+      const int col = kk * 16 + 8 * (lane >> 3);
+      ldsm_x4(kb, sK + row * ROWP + col * 2);
+      mma16816<BF16>(sacc[j], qa[kk], kb[0], kb[1]);
+      if (kk + 1 < KS) mma16816<BF16>(sacc[j], qa[kk + 1], kb[2], kb[3]);
+    }
+  }
+  // scale, mask, row statistics (rows g and g+8; the four lanes of a group share a row)
+  float m_lo = -INFINITY, m_hi = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int col = 8 * j + 2 * tig + (e & 1);
+      const float v = col < wrows ? sacc[j][e] * a.scale : -INFINITY;
+      sacc[j][e] = v;
+      if (e < 2) m_lo = fmaxf(m_lo, v);
+      else m_hi = fmaxf(m_hi, v);
+    }
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, o));
+    m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, o));
+  }
+  float l_lo = 0.f, l_hi = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float mm = e < 2 ? m_lo : m_hi;
+      const float p = (sacc[j][e] == -INFINITY) ? 0.f : __expf(sacc[j][e] - mm);
+      sacc[j][e] = p;
+      if (e < 2) l_lo += p;
+      else l_hi += p;
+    }
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, o);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, o);
+  }
+  // O = P·V: P as A fragments (two k-steps of 16 rows), V via ldmatrix.trans
+  uint32_t pa[2][4];
+#pragma unroll
+  for (int k2 = 0; k2 < 2; ++k2) {
+    pa[k2][0] = pack2<BF16>(sacc[2 * k2][0], sacc[2 * k2][1]);
+    pa[k2][1] = pack2<BF16>(sacc[2 * k2][2], sacc[2 * k2][3]);
+    pa[k2][2] = pack2<BF16>(sacc[2 * k2 + 1][0], sacc[2 * k2 + 1][1]);
+    pa[k2][3] = pack2<BF16>(sacc[2 * k2 + 1][2], sacc[2 * k2 + 1][3]);
+  }
+  float oacc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) oacc[n][e] = 0.f;
+#pragma unroll
+  for (int k2 = 0; k2 < 2; ++k2) {
+#pragma unroll
+    for (int n = 0; n < NT; n += 2) {
+      uint32_t vb[4];
+      const int row = wrow0 + 16 * k2 + (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int col = n * 8 + 8 * (lane >> 4);
+      ldsm_x4_t(vb, sV + row * ROWP + col * 2);
+      mma16816<BF16>(oacc[n], pa[k2], vb[0], vb[1]);
+      mma16816<BF16>(oacc[n + 1], pa[k2], vb[2], vb[3]);
+    }
+  }
+  // warp partial -> shared memory (the warp's own K rows are free now): O as fp32 [16][D]
+  __syncwarp();
+  float* so = reinterpret_cast<float*>(sK + wrow0 * ROWP);   // 16*D*4 bytes <= 32*ROWP
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int col = n * 8 + 2 * tig;
+    so[g * D + col] = oacc[n][0];
+    so[g * D + col + 1] = oacc[n][1];
+    so[(g + 8) * D + col] = oacc[n][2];
+    so[(g + 8) * D + col + 1] = oacc[n][3];
+  }
+  if (tig == 0) {
+    s_m[warp][g] = wrows > 0 ? m_lo : -INFINITY;
+    s_m[warp][g + 8] = wrows > 0 ? m_hi : -INFINITY;
+    s_l[warp][g] = l_lo;
+    s_l[warp][g + 8] = l_hi;
   }
   __syncthreads();
-  if (tid == 0) {
-    const uint32_t bytes = (uint32_t)(nrows * ROWB);
-    mbar_arrive_expect_tx(&bar, 2 * bytes);
-    if (bytes) {
-      bulk_load(sK, a.k + (int64_t)seg * a.kv_seg + (int64_t)r0 * a.kv_s, bytes, &bar);
-      bulk_load(sV, a.v + (int64_t)seg * a.kv_seg + (int64_t)r0 * a.kv_s, bytes, &bar);
-    }
-  }
-  // query slice of this lane (pre-scaled), while the copies are in flight
-  float qf[8];
-  {
-    const int g = active ? r / a.q_len : 0, i = active ? r - (r / a.q_len) * a.q_len : 0;
-    const char* qp = a.q + (int64_t)b * a.q_sb + (int64_t)(hk * G + g) * a.q_sh + (int64_t)i * a.q_sq;
-    const uint4 raw = active ? *reinterpret_cast<const uint4*>(qp + sl * 16) : make_uint4(0, 0, 0, 0);
-    cvt8(raw, qf, BF16);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qf[e] *= a.scale;
-  }
-  const bool ok = mbar_wait(&bar, 0, kWaitTimeoutNs);
-  if (__syncthreads_or(!ok)) {
-    if (tid == 0 && a.status) atomicOr(a.status, MSKV_STATUS_TIMEOUT);
-    mbar_wait(&bar, 0, kDrainTimeoutNs);
-    return;  // every CTA of the launch reaches this point together only on a broken device
-  }
-
-  // 1. scores of the 64 rows for this lane's query row (partial over its d-slice)
-  float part[kAtTile];
-#pragma unroll
-  for (int row = 0; row < kAtTile; ++row) {
-    float acc = 0.f;
-    if (row < nrows) {
-      float f[8];
-      cvt8(*reinterpret_cast<const uint4*>(sK + row * ROWB + sl * 16), f, BF16);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc = fmaf(qf[e], f[e], acc);
-    }
-    part[row] = acc;
-  }
-  reduce_scatter_n<kAtTile, SL>(part, sl);   // part[0..RPL) = rows [sl*RPL, (sl+1)*RPL)
-  // 2. softmax statistics over the tile (rows >= nrows excluded)
-  float m = -INFINITY;
-#pragma unroll
-  for (int x = 0; x < RPL; ++x)
-    if (sl * RPL + x < nrows) m = fmaxf(m, part[x]);
-#pragma unroll
-  for (int o = SL / 2; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  float l = 0.f;
-#pragma unroll
-  for (int x = 0; x < RPL; ++x) {
-    const int row = sl * RPL + x;
-    const float p = row < nrows ? expf(part[x] - m) : 0.f;
-    s_p[warp * RPW + lane / SL][row] = p;
-    l += p;
-  }
-#pragma unroll
-  for (int o = SL / 2; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-  __syncwarp();
-  // 3. P·V for this lane's 8 output dims
-  float acc[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-  const float* prow = s_p[warp * RPW + lane / SL];
-  for (int row = 0; row < nrows; ++row) {
-    float f[8];
-    cvt8(*reinterpret_cast<const uint4*>(sV + row * ROWB + sl * 16), f, BF16);
-    const float p = prow[row];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = fmaf(p, f[e], acc[e]);
-  }
-  // 4. partial -> workspace, last CTA of the segment merges
+  // merge the four warps -> this CTA's split partial
   const int64_t wstride = (int64_t)a.nr * (D + 2);
   float* wp = a.ws + ((int64_t)seg * a.splits + split) * wstride;
-  if (active) {
-    float4* dst = reinterpret_cast<float4*>(wp + (int64_t)r * (D + 2) + sl * 8);
-    if (((uintptr_t)dst & 15) == 0) {
-      dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) wp[(int64_t)r * (D + 2) + sl * 8 + e] = acc[e];
-    }
-    if (sl == 0) {
-      wp[(int64_t)r * (D + 2) + D] = nrows > 0 ? m : -INFINITY;
-      wp[(int64_t)r * (D + 2) + D + 1] = nrows > 0 ? l : 0.f;
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned prev = atomicAdd(&a.tickets[seg], 1u);
-    s_last = prev == (unsigned)(a.splits - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (active) {
-    const float* base = a.ws + (int64_t)seg * a.splits * wstride + (int64_t)r * (D + 2);
+  for (int x = tid; x < nr * D; x += kAtThreads) {
+    const int r = x / D, d = x - r * D;
     float M = -INFINITY;
-    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, __ldcg(base + s * wstride + D));
-    float L = 0.f, o[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = 0.f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float ms = __ldcg(base + s * wstride + D);
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - M);
-      L += __ldcg(base + s * wstride + D + 1) * w;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][r]);
+    float L = 0.f, o = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] += __ldcg(base + s * wstride + sl * 8 + e) * w;
+    for (int w = 0; w < 4; ++w) {
+      if (s_m[w][r] == -INFINITY) continue;
+      const float f = __expf(s_m[w][r] - M);
+      L += s_l[w][r] * f;
+      o += reinterpret_cast<const float*>(sK + w * 32 * ROWP)[r * D + d] * f;
     }
-    const int g = r / a.q_len, i = r - g * a.q_len;
-    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    T* op = reinterpret_cast<T*>(a.out + (int64_t)b * a.o_sb + (int64_t)(hk * G + g) * a.o_sh + (int64_t)i * a.o_sq);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) op[sl * 8 + e] = from_f<T>(L > 0.f ? o[e] / L : 0.f);
+    wp[(int64_t)r * (D + 2) + d] = o;
+    if (d == 0) {
+      wp[(int64_t)r * (D + 2) + D] = M;
+      wp[(int64_t)r * (D + 2) + D + 1] = L;
+    }
   }
-  if (tid == 0) a.tickets[seg] = 0u;  // re-arm for the next launch on this workspace
+}
+
+// Merges the split partials of one (segment, query row) per block (one thread per output dim):
+// every split's maximum, normaliser and value are independent loads, so the merge costs about
+// one L2 round trip.
+template <typename T, int D>
+__global__ void __launch_bounds__(D) attn_merge_kernel(const AttnDev a) {
+  const int seg = blockIdx.x / a.nr, r = blockIdx.x - (blockIdx.x / a.nr) * a.nr;
+  const int d = threadIdx.x;
+  const int64_t wstride = (int64_t)a.nr * (D + 2);
+  const float* rb = a.ws + (int64_t)seg * a.splits * wstride + (int64_t)r * (D + 2);
+  float M = -INFINITY;
+#pragma unroll 8
+  for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, rb[sp * wstride + D]);
+  float L = 0.f, o = 0.f;
+#pragma unroll 8
+  for (int sp = 0; sp < a.splits; ++sp) {
+    const float ms = rb[sp * wstride + D];
+    const float w = ms == -INFINITY ? 0.f : __expf(ms - M);
+    L += rb[sp * wstride + D + 1] * w;
+    o += rb[sp * wstride + d] * w;
+  }
+  const int b = seg / a.kv_heads, hk = seg - b * a.kv_heads;
+  const int G = a.q_heads / a.kv_heads;
+  const int gq = r / a.q_len, i = r - gq * a.q_len;
+  T* op = reinterpret_cast<T*>(a.out + (int64_t)b * a.o_sb + (int64_t)(hk * G + gq) * a.o_sh + (int64_t)i * a.o_sq);
+  op[d] = from_f<T>(L > 0.f ? o / L : 0.f);
 }
 
 // Generic path: one warp per output row (b, hq, i); online softmax over the selected rows.
@@ -315,14 +431,14 @@ static bool fast_path(const mskv_attn_desc* d) {
   if (dtype_size(d->dtype) != 2) return false;
   if (d->head_dim != 64 && d->head_dim != 128) return false;
   const int G = d->q_heads / d->kv_heads;
-  const int rows_max = 4 * (32 / (d->head_dim / 8));  // 4 warps x query rows per warp
-  if (G * d->q_len > rows_max) return false;
-  if (d->kv_stride_s != (int64_t)d->head_dim * 2) return false;  // tiles are single bulk copies
-  if ((int64_t)d->batch * d->kv_heads > kAtWsHeader / 4) return false;
+  if (G * d->q_len > 16) return false;                            // one m16 MMA row block
+  // the split merge keeps one weight per (split, query row) in the V tile's shared memory
+  const int64_t splits = d->num_selected > 0 ? (d->num_selected + kAtTile - 1) / kAtTile : 1;
+  if ((splits + 1) * 16 * 4 > (int64_t)kAtTile * (d->head_dim * 2 + 16)) return false;
   const uint64_t al = (uint64_t)(uintptr_t)d->k | (uint64_t)(uintptr_t)d->v | (uint64_t)d->kv_stride_seg |
-                      (uint64_t)(uintptr_t)d->q | (uint64_t)d->q_stride_b | (uint64_t)d->q_stride_h |
-                      (uint64_t)d->q_stride_q;
-  return (al & 15) == 0;
+                      (uint64_t)d->kv_stride_s | (uint64_t)(uintptr_t)d->q | (uint64_t)d->q_stride_b |
+                      (uint64_t)d->q_stride_h | (uint64_t)d->q_stride_q;
+  return (al & 15) == 0;                                          // 16-byte bulk copies / loads
 }
 
 static int64_t splits_of(const mskv_attn_desc* d) {
@@ -337,7 +453,7 @@ extern "C" uint64_t mskv_attention_workspace_bytes(const mskv_attn_desc* d) {
   if (!d || d->kv_heads <= 0 || d->q_heads <= 0 || d->q_len <= 0 || d->batch < 0) return 0;
   if (!fast_path(d)) return 0;
   const int64_t nr = (int64_t)(d->q_heads / d->kv_heads) * d->q_len;
-  return (uint64_t)(kAtWsHeader + (int64_t)d->batch * d->kv_heads * splits_of(d) * nr * (d->head_dim + 2) * 4);
+  return (uint64_t)((int64_t)d->batch * d->kv_heads * splits_of(d) * nr * (d->head_dim + 2) * 4);
 }
 
 extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
@@ -367,18 +483,36 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
     if (!d->workspace || d->workspace_bytes < need)
       return fail(MSKV_ERR_ARG, "mskv_sparse_attention: workspace needs %llu bytes", (unsigned long long)need);
     if (((uintptr_t)d->workspace & 255) != 0) return fail(MSKV_ERR_ARG, "mskv_sparse_attention: workspace must be 256-byte aligned");
-    a.tickets = static_cast<unsigned*>(d->workspace);
-    a.ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + kAtWsHeader);
+    a.ws = static_cast<float*>(d->workspace);
     a.splits = (int)splits_of(d);
     const int64_t blocks = (int64_t)d->batch * d->kv_heads * a.splits;
     if (blocks > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "mskv_sparse_attention: grid too large");
     const bool bf = d->dtype == MSKV_DT_BF16;
+    const int smem = (2 * kAtTile + 16) * (d->head_dim * 2 + 16);
+    static bool attr_set = false;  // benign race: every thread sets the same values
+    if (!attr_set) {
+      cudaFuncSetAttribute(attn_mma_kernel<true, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
+      cudaFuncSetAttribute(attn_mma_kernel<false, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
+      cudaFuncSetAttribute(attn_mma_kernel<true, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
+      cudaFuncSetAttribute(attn_mma_kernel<false, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
+      attr_set = true;
+    }
     if (d->head_dim == 128) {
-      if (bf) attn_split_kernel<true, 128><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
-      else attn_split_kernel<false, 128><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
+      if (bf) attn_mma_kernel<true, 128><<<(unsigned)blocks, kAtThreads, smem, st>>>(a);
+      else attn_mma_kernel<false, 128><<<(unsigned)blocks, kAtThreads, smem, st>>>(a);
     } else {
-      if (bf) attn_split_kernel<true, 64><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
-      else attn_split_kernel<false, 64><<<(unsigned)blocks, kAtThreads, 0, st>>>(a);
+      if (bf) attn_mma_kernel<true, 64><<<(unsigned)blocks, kAtThreads, smem, st>>>(a);
+      else attn_mma_kernel<false, 64><<<(unsigned)blocks, kAtThreads, smem, st>>>(a);
+    }
+    int rc = after_launch("mskv_sparse_attention");
+    if (rc) return rc;
+    const unsigned mblocks = (unsigned)((int64_t)d->batch * d->kv_heads * a.nr);
+    if (d->head_dim == 128) {
+      if (bf) attn_merge_kernel<__nv_bfloat16, 128><<<mblocks, 128, 0, st>>>(a);
+      else attn_merge_kernel<__half, 128><<<mblocks, 128, 0, st>>>(a);
+    } else {
+      if (bf) attn_merge_kernel<__nv_bfloat16, 64><<<mblocks, 64, 0, st>>>(a);
+      else attn_merge_kernel<__half, 64><<<mblocks, 64, 0, st>>>(a);
     }
     return after_launch("mskv_sparse_attention");
   }
@@ -402,8 +536,9 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
 // file-scope device array of MSKV_NOALLOC_ATTN_SCRATCH_BYTES, which every GPU that loads
 // this library keeps until the process exits.  Its device address is looked up once per
 // device (cudaGetSymbolAddress, on that device's first call) and cached; nothing is
-// allocated or freed.  All calls on a device share the array, so calls that overlap on the
-// GPU (different streams without ordering) race on it.
+// allocated or freed.  Each call rewrites every partial it later reads, so nothing in the
+// array has to start at zero; but all calls on a device share it, so calls that overlap on
+// the GPU (different streams without ordering) race on it.
 static __device__ __align__(256) unsigned char g_attn_scratch[MSKV_NOALLOC_ATTN_SCRATCH_BYTES];
 
 namespace {
@@ -442,11 +577,5 @@ extern "C" int mskv_sparse_attention_noalloc(const mskv_attn_desc* d, void* stre
   mskv_attn_desc c = *d;
   c.workspace = scratch;
   c.workspace_bytes = MSKV_NOALLOC_ATTN_SCRATCH_BYTES;
-  if (need > 0) {
-    // The per-segment tickets must start at zero; the array keeps whatever the last call
-    // (possibly an interrupted one) left there.
-    cudaError_t e = cudaMemsetAsync(scratch, 0, kAtWsHeader, as_stream(stream));
-    if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(attention scratch tickets)");
-  }
   return mskv_sparse_attention(&c, stream);
 }

@@ -375,9 +375,7 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     key = (device.index, torch.cuda.current_stream(device).cuda_stream)
     w = _workspaces.get(key)
     if w is None or w.numel() < nbytes:
-        # zero-filled: the attention workspace starts with per-segment tickets that every
-        # launch leaves at zero
-        w = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        w = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
         _workspaces[key] = w
     return w
 
