@@ -226,7 +226,6 @@ __device__ __forceinline__ uint64_t block_exclusive_scan_n(uint64_t v, uint64_t*
 __global__ void __cluster_dims__(kTcCtas, 1, 1) __launch_bounds__(kTcThreads)
     topk_cluster_kernel(const TopkDev a) {
   extern __shared__ uint32_t s_keys[];
-  __shared__ uint32_t s_whist[kTcWarps][256];
   __shared__ uint32_t s_hist[4][256];
   __shared__ uint32_t s_tot[256];
   __shared__ uint32_t s_prefix, s_krem;
@@ -253,11 +252,11 @@ __global__ void __cluster_dims__(kTcCtas, 1, 1) __launch_bounds__(kTcThreads)
   uint32_t prefix = 0, mask = 0, krem = (uint32_t)K;
   if (K > 0 && K < n) {
     for (int i = tid; i < m; i += kTcThreads) s_keys[i] = key_at(a, row0, lo + i);
+    for (int i = tid; i < 4 * 256; i += kTcThreads) (&s_hist[0][0])[i] = 0;   // one histogram per pass
     __syncthreads();
     for (int pass = 0; pass < 4; ++pass) {
       const int shift = 24 - 8 * pass;
-      for (int i = tid; i < kTcWarps * 256; i += kTcThreads) (&s_whist[0][0])[i] = 0;
-      __syncthreads();
+      // histogram of this pass's digit; equal digits within a warp are merged before the atomic
       for (int base = 0; base < m; base += kTcThreads) {
         const int i = base + tid;
         uint32_t bin = 0xffffffffu;
@@ -266,16 +265,9 @@ __global__ void __cluster_dims__(kTcCtas, 1, 1) __launch_bounds__(kTcThreads)
           if ((key & mask) == prefix) bin = (key >> shift) & 255u;
         }
         const uint32_t peers = __match_any_sync(0xffffffffu, bin);
-        if (bin != 0xffffffffu && lane == __ffs(peers) - 1) atomicAdd(&s_whist[warp][bin], __popc(peers));
+        if (bin != 0xffffffffu && lane == __ffs(peers) - 1) atomicAdd(&s_hist[pass][bin], __popc(peers));
       }
-      __syncthreads();
-      if (tid < 256) {
-        uint32_t s = 0;
-#pragma unroll
-        for (int ww = 0; ww < kTcWarps; ++ww) s += s_whist[ww][tid];
-        s_hist[pass][tid] = s;
-      }
-      cluster.sync();
+      cluster.sync();   // orders every CTA's histogram before the distributed reads
       if (tid < 256) {
         uint32_t s = 0;
 #pragma unroll
