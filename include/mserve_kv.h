@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define MSKV_ABI_VERSION 1
+#define MSKV_ABI_VERSION 2
 
 /* ---- return codes ---------------------------------------------------------------------- */
 #define MSKV_OK 0
@@ -202,8 +202,11 @@ int mskv_score(const mskv_score_desc* d, void* stream);
  * Replaces the selection half of compute_token_importance
  * (qwen-eljrte/Qwen_Transformer/attention.py:567-572, torch.topk) and adds the recent window.
  * Selection j (b = j / sel_per_batch) ranks the key
- *   key(t) = scale * sum_{r<rows_per_sel} scores[(j*rows_per_sel + r)*scores_stride + t]
- * (fp32, summed in r order) over the candidates t in [0, n), n = max(L - recent, 0),
+ *   key(t) = scale * sum_{r<rows_per_sel} scores[row(j, r) + t],
+ *   row(j, r) = j*sel_stride + (r / row_block)*block_stride + (r % row_block)*scores_stride
+ * (fp32, summed in r order; sel_stride 0 means rows_per_sel*scores_stride and row_block 0
+ * means rows_per_sel, i.e. the rows of a selection are consecutive at scores_stride), over
+ * the candidates t in [0, n), n = max(L - recent, 0),
  * L = len[b] (NULL: len_scalar), keeps the top k = min(top_k[b] or top_k_scalar, n) by key
  * (ties broken toward the lower token index, NaN ranks highest), and appends the window
  * [n, L).  The output row idx[j*out_stride ...] is sorted ascending and holds
@@ -228,7 +231,14 @@ typedef struct mskv_topk_desc {
   int32_t rows_per_sel;
   int32_t sel_per_batch;
   int32_t out_bits;             /* 32 or 64                                           */
+  int32_t row_block;            /* rows per block (0: rows_per_sel)                   */
+  int64_t sel_stride;           /* elements (0: rows_per_sel * scores_stride)         */
+  int64_t block_stride;         /* elements between row blocks                        */
 } mskv_topk_desc;
+/* The blocked row layout serves selections shared by KV heads that are sharded over
+ * ranks: each rank's per-head score rows [B, Hl, T] all-gathered into [ranks, B, Hl, T]
+ * are summed in global head order with sel_stride = Hl*T, row_block = Hl,
+ * scores_stride = T, block_stride = B*Hl*T and rows_per_sel = ranks*Hl. */
 int mskv_topk(const mskv_topk_desc* d, void* stream);
 
 /* ---- sparse decode attention over the selected rows ---------------------------------------

@@ -79,6 +79,7 @@ class TopkDesc(C.Structure):
         ("counts", _vp), ("len", _vp), ("top_k", _vp), ("status", _vp),
         ("scale", C.c_float), ("len_scalar", _i32), ("top_k_scalar", _i32), ("recent", _i32),
         ("num_sel", _i32), ("rows_per_sel", _i32), ("sel_per_batch", _i32), ("out_bits", _i32),
+        ("row_block", _i32), ("sel_stride", _i64), ("block_stride", _i64),
     ]
 
 
@@ -128,7 +129,7 @@ def lib() -> C.CDLL:
             fn = getattr(h, name)
             fn.restype = res
             fn.argtypes = args
-        if h.mskv_abi_version() != 1:
+        if h.mskv_abi_version() != 2:
             raise ImportError(f"{LIB_PATH}: unexpected ABI version {h.mskv_abi_version()}")
         _lib = h
     return _lib

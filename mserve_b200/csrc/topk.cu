@@ -35,7 +35,8 @@ struct TopkDev {
   const int32_t* len;
   const int32_t* topk;
   float scale;
-  int32_t len_scalar, k_scalar, recent, num_sel, rows_per_sel, sel_per_batch, out64;
+  int32_t len_scalar, k_scalar, recent, num_sel, rows_per_sel, sel_per_batch, out64, row_block;
+  int64_t sel_stride, block_stride;
 };
 
 // Order-preserving map fp32 -> uint32.  Every NaN (either sign, any payload) maps to the
@@ -46,9 +47,11 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Summed score of token t over the selection's rows, in row order (row 0 at row0).
 __device__ __forceinline__ uint32_t key_at(const TopkDev& a, const float* row0, int64_t t) {
   float s = row0[t];
-  for (int r = 1; r < a.rows_per_sel; ++r) s += row0[(int64_t)r * a.ss + t];
+  for (int r = 1; r < a.rows_per_sel; ++r)
+    s += row0[(int64_t)(r / a.row_block) * a.block_stride + (int64_t)(r % a.row_block) * a.ss + t];
   return order_key(s * a.scale);
 }
 
@@ -96,7 +99,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_kernel(const TopkDev a) {
   if (K < 0) K = 0;
   if (K > n) K = n;
   const int64_t w = L - n;  // recent window [n, L)
-  const float* row0 = a.scores + j * a.rows_per_sel * a.ss;
+  const float* row0 = a.scores + j * a.sel_stride;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
   uint32_t prefix = 0, mask = 0, krem = (uint32_t)K;
@@ -187,50 +190,53 @@ __global__ void __launch_bounds__(kTkThreads) topk_kernel(const TopkDev a) {
 // Cluster path: 8 CTAs (one thread-block cluster) per selection.
 //
 // CTA r of the cluster owns the r-th eighth of the candidates and keeps their keys in shared
-// memory (loaded once).  Each radix pass builds the CTA's 256-bin histogram, then every CTA
-// sums the eight histograms through distributed shared memory (each pass has its own
-// histogram buffer, so one cluster barrier per pass suffices) and finds the same digit.  The
-// ordered compaction exchanges the per-CTA (#greater, #equal) counts the same way, so each
-// CTA writes its part of the ascending output directly.
+// memory.  The first digit's histogram is built while the keys are loaded.  Each radix pass
+// ends with every CTA summing the eight histograms through distributed shared memory (one
+// buffer per pass, so one cluster barrier per pass) and finding the same digit with a
+// 256-thread suffix scan.  Passes 1-3 visit only the keys that still match the prefix: pass 1
+// appends the keys matching the first digit to a survivor list, pass 2 filters that list
+// again, so the last passes touch a handful of keys.  The ordered compaction gives each warp a
+// contiguous run of keys, counts with ballots, exchanges the per-CTA (#greater, #equal)
+// counts through distributed shared memory and writes the ascending output directly.
 constexpr int kTcCtas = 8;
 constexpr int kTcThreads = 512;
 constexpr int kTcWarps = kTcThreads / 32;
-constexpr int kTcMaxKeys = 16384;  // keys per CTA held in shared memory (64 KB)
+constexpr int kTcMaxKeys = 16384;  // keys per CTA; shared memory holds them plus two survivor lists
 
-template <int NW>
-__device__ __forceinline__ uint64_t block_exclusive_scan_n(uint64_t v, uint64_t* warp_tot, uint64_t* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint64_t inc = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint64_t n = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += n;
-  }
-  if (lane == 31) warp_tot[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    uint64_t w = lane < NW ? warp_tot[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint64_t n = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += n;
-    }
-    if (lane < NW) warp_tot[lane] = w;
-  }
-  __syncthreads();
-  *total = warp_tot[NW - 1];
-  const uint64_t before_warp = warp ? warp_tot[warp - 1] : 0;
-  return before_warp + inc - v;
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Histogram of one digit (bin 0xffffffff = no contribution).  Plain shared atomics: merging
+// equal digits of a warp with __match_any_sync first was slower on both spread-out and
+// tie-heavy scores.
+__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, int) {
+  if (bin != 0xffffffffu) atomicAdd(&hist[bin], 1u);
+}
+
+// Appends `key` to list[*count] for lanes with keep set (warp-aggregated).
+__device__ __forceinline__ void list_push(uint32_t* list, uint32_t* count, bool keep, uint32_t key, int lane) {
+  const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+  if (!bal) return;
+  uint32_t base = 0;
+  if (lane == 0) base = atomicAdd(count, (uint32_t)__popc(bal));
+  base = __shfl_sync(0xffffffffu, base, 0);
+  if (keep) list[base + __popc(bal & lanemask_lt())] = key;
 }
 
 __global__ void __cluster_dims__(kTcCtas, 1, 1) __launch_bounds__(kTcThreads)
-    topk_cluster_kernel(const TopkDev a) {
-  extern __shared__ uint32_t s_keys[];
+    topk_cluster_kernel(const TopkDev a, int cap) {
+  extern __shared__ uint32_t s_dyn[];
   __shared__ uint32_t s_hist[4][256];
-  __shared__ uint32_t s_tot[256];
-  __shared__ uint32_t s_prefix, s_krem;
+  __shared__ uint32_t s_wsuf[8];
+  __shared__ uint32_t s_prefix, s_krem, s_n1, s_n2;
+  __shared__ uint64_t s_wcnt[kTcWarps];
   __shared__ uint64_t s_cnt;
-  __shared__ uint64_t s_scan[kTcWarps];
+  uint32_t* s_keys = s_dyn;            // this CTA's keys, in token order
+  uint32_t* s_l1 = s_dyn + cap;        // keys matching the first digit
+  uint32_t* s_l2 = s_dyn + 2 * cap;    // keys matching the first two digits
 
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
@@ -242,90 +248,116 @@ __global__ void __cluster_dims__(kTcCtas, 1, 1) __launch_bounds__(kTcThreads)
   if (K < 0) K = 0;
   if (K > n) K = n;
   const int64_t w = L - n;
-  const float* row0 = a.scores + j * a.rows_per_sel * a.ss;
+  const float* row0 = a.scores + j * a.sel_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t chunk = (n + kTcCtas - 1) / kTcCtas;
   const int64_t lo = min((int64_t)rank * chunk, n);
   const int64_t hi = min(lo + chunk, n);
   const int m = (int)(hi - lo);
 
-  uint32_t prefix = 0, mask = 0, krem = (uint32_t)K;
   if (K > 0 && K < n) {
-    for (int i = tid; i < m; i += kTcThreads) s_keys[i] = key_at(a, row0, lo + i);
-    for (int i = tid; i < 4 * 256; i += kTcThreads) (&s_hist[0][0])[i] = 0;   // one histogram per pass
+    for (int i = tid; i < 4 * 256; i += kTcThreads) (&s_hist[0][0])[i] = 0;
+    if (tid == 0) { s_n1 = 0; s_n2 = 0; }
     __syncthreads();
+    for (int i = tid; i < m; i += kTcThreads) s_keys[i] = key_at(a, row0, lo + i);
+    // first digit's histogram: each thread reads back the keys it stored itself
+    for (int base = 0; base < m; base += kTcThreads) {
+      const int i = base + tid;
+      hist_add(s_hist[0], i < m ? s_keys[i] >> 24 : 0xffffffffu, lane);
+    }
+    uint32_t prefix = 0, krem = (uint32_t)K;
     for (int pass = 0; pass < 4; ++pass) {
       const int shift = 24 - 8 * pass;
-      // histogram of this pass's digit; equal digits within a warp are merged before the atomic
-      for (int base = 0; base < m; base += kTcThreads) {
-        const int i = base + tid;
-        uint32_t bin = 0xffffffffu;
-        if (i < m) {
-          const uint32_t key = s_keys[i];
-          if ((key & mask) == prefix) bin = (key >> shift) & 255u;
+      if (pass > 0) {
+        const uint32_t mask = 0xffffffffu << (shift + 8);
+        if (pass == 1) {          // all keys; survivors of digit 0 go to list 1
+          for (int base = 0; base < m; base += kTcThreads) {
+            const int i = base + tid;
+            const uint32_t key = i < m ? s_keys[i] : 0u;
+            const bool keep = i < m && (key & mask) == prefix;
+            hist_add(s_hist[1], keep ? (key >> shift) & 255u : 0xffffffffu, lane);
+            list_push(s_l1, &s_n1, keep, key, lane);
+          }
+        } else if (pass == 2) {   // list 1; survivors of digits 0-1 go to list 2
+          const int n1 = (int)s_n1;
+          for (int base = 0; base < n1; base += kTcThreads) {
+            const int i = base + tid;
+            const uint32_t key = i < n1 ? s_l1[i] : 0u;
+            const bool keep = i < n1 && (key & mask) == prefix;
+            hist_add(s_hist[2], keep ? (key >> shift) & 255u : 0xffffffffu, lane);
+            list_push(s_l2, &s_n2, keep, key, lane);
+          }
+        } else {                  // list 2
+          const int n2 = (int)s_n2;
+          for (int base = 0; base < n2; base += kTcThreads) {
+            const int i = base + tid;
+            const uint32_t key = i < n2 ? s_l2[i] : 0u;
+            const bool keep = i < n2 && (key & mask) == prefix;
+            hist_add(s_hist[3], keep ? key & 255u : 0xffffffffu, lane);
+          }
         }
-        const uint32_t peers = __match_any_sync(0xffffffffu, bin);
-        if (bin != 0xffffffffu && lane == __ffs(peers) - 1) atomicAdd(&s_hist[pass][bin], __popc(peers));
       }
-      cluster.sync();   // orders every CTA's histogram before the distributed reads
+      cluster.sync();   // every CTA's histogram (and this CTA's lists) complete
+      // digit search: bin t's count summed over the cluster; suffix sums over higher bins
+      uint32_t c = 0, suf = 0;
       if (tid < 256) {
-        uint32_t s = 0;
 #pragma unroll
-        for (int c = 0; c < kTcCtas; ++c) s += *cluster.map_shared_rank(&s_hist[pass][tid], c);
-        s_tot[tid] = s;
-      }
-      __syncthreads();
-      if (warp == 0) {
-        uint32_t c[8], lt = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) { c[i] = s_tot[lane * 8 + i]; lt += c[i]; }
-        uint32_t suf = lt;
+        for (int r = 0; r < kTcCtas; ++r) c += *cluster.map_shared_rank(&s_hist[pass][tid], r);
+        suf = c;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
           if (lane + o < 32) suf += v;
         }
-        uint32_t cum = suf - lt;
-#pragma unroll
-        for (int i = 7; i >= 0; --i) {
-          if (cum < krem && cum + c[i] >= krem) {
-            s_prefix = prefix | ((uint32_t)(lane * 8 + i) << shift);
-            s_krem = krem - cum;
-          }
-          cum += c[i];
+        if (lane == 0) s_wsuf[warp] = suf;
+      }
+      __syncthreads();
+      if (tid < 256) {
+        uint32_t above = suf - c;
+        for (int w2 = warp + 1; w2 < 8; ++w2) above += s_wsuf[w2];
+        if (above < krem && above + c >= krem) {
+          s_prefix = prefix | ((uint32_t)tid << shift);
+          s_krem = krem - above;
         }
       }
       __syncthreads();
       prefix = s_prefix;
       krem = s_krem;
-      mask |= 0xffu << shift;
     }
-    // Ordered compaction.  Thread i owns the contiguous run [i*E, (i+1)*E) of this CTA's keys.
-    const int E = (m + kTcThreads - 1) / kTcThreads;
-    const int i_lo = min(tid * E, m), i_hi = min(i_lo + E, m);
+    // Ordered compaction.  Warp v owns the contiguous run [v*R, (v+1)*R) of this CTA's keys.
+    const int R = ((m + kTcThreads - 1) / kTcThreads) * 32;
+    const int w_lo = min(warp * R, m), w_hi = min(w_lo + R, m);
     uint32_t gt = 0, eq = 0;
-    for (int i = i_lo; i < i_hi; ++i) {
-      gt += s_keys[i] > prefix;
-      eq += s_keys[i] == prefix;
+    for (int base = w_lo; base < w_hi; base += 32) {
+      const int i = base + lane;
+      const uint32_t key = i < w_hi ? s_keys[i] : 0u;
+      gt += __popc(__ballot_sync(0xffffffffu, i < w_hi && key > prefix));
+      eq += __popc(__ballot_sync(0xffffffffu, i < w_hi && key == prefix));
     }
-    uint64_t cta_total;
-    const uint64_t before = block_exclusive_scan_n<kTcWarps>(((uint64_t)gt << 32) | eq, s_scan, &cta_total);
+    if (lane == 0) s_wcnt[warp] = ((uint64_t)gt << 32) | eq;
+    __syncthreads();
+    uint64_t warp_before = 0, cta_total = 0;
+    for (int v = 0; v < kTcWarps; ++v) {
+      const uint64_t x = s_wcnt[v];
+      if (v < warp) warp_before += x;
+      cta_total += x;
+    }
     if (tid == 0) s_cnt = cta_total;
     cluster.sync();
-    uint64_t cta_before = 0;
-    for (int c = 0; c < rank; ++c) cta_before += *cluster.map_shared_rank(&s_cnt, c);
-    const uint64_t all_before = cta_before + before;
-    const uint32_t gt_before = (uint32_t)(all_before >> 32);
-    uint32_t eq_seen = (uint32_t)(all_before & 0xffffffffu);
-    int64_t pos = (int64_t)gt_before + min(eq_seen, krem);
-    for (int i = i_lo; i < i_hi; ++i) {
-      const uint32_t key = s_keys[i];
-      if (key > prefix) {
-        put(a, j, pos++, lo + i);
-      } else if (key == prefix) {
-        if (eq_seen < krem) put(a, j, pos++, lo + i);
-        ++eq_seen;
-      }
+    uint64_t before = warp_before;
+    for (int r = 0; r < rank; ++r) before += *cluster.map_shared_rank(&s_cnt, r);
+    uint32_t gtb = (uint32_t)(before >> 32), eqb = (uint32_t)(before & 0xffffffffu);
+    const uint32_t lt = lanemask_lt();
+    for (int base = w_lo; base < w_hi; base += 32) {
+      const int i = base + lane;
+      const uint32_t key = i < w_hi ? s_keys[i] : 0u;
+      const bool g = i < w_hi && key > prefix;
+      const bool e = i < w_hi && key == prefix;
+      const uint32_t bg = __ballot_sync(0xffffffffu, g), be = __ballot_sync(0xffffffffu, e);
+      const uint32_t my_gt = gtb + __popc(bg & lt), my_eq = eqb + __popc(be & lt);
+      if (g || (e && my_eq < krem)) put(a, j, (int64_t)my_gt + min(my_eq, krem), lo + i);
+      gtb += __popc(bg);
+      eqb += __popc(be);
     }
   } else if (K == n) {
     for (int64_t t = lo + tid; t < hi; t += kTcThreads) put(a, j, t, t);
@@ -356,6 +388,11 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
   a.len_scalar = d->len_scalar; a.k_scalar = d->top_k_scalar; a.recent = d->recent;
   a.num_sel = d->num_sel; a.rows_per_sel = d->rows_per_sel; a.sel_per_batch = d->sel_per_batch;
   a.out64 = d->out_bits == 64;
+  if (d->row_block < 0 || d->sel_stride < 0 || d->block_stride < 0)
+    return fail(MSKV_ERR_ARG, "mskv_topk: negative row layout");
+  a.row_block = d->row_block > 0 ? d->row_block : d->rows_per_sel;
+  a.sel_stride = d->sel_stride > 0 ? d->sel_stride : (int64_t)d->rows_per_sel * d->scores_stride;
+  a.block_stride = d->block_stride;
   // len_scalar bounds every len[b]; it sizes the per-CTA key buffer of the cluster path.
   const int64_t n_max = d->len_scalar > d->recent ? (int64_t)d->len_scalar - d->recent : 0;
   const int64_t keys_per_cta = (n_max + kTcCtas - 1) / kTcCtas;
@@ -363,11 +400,12 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
     static bool attr_set = false;  // benign race: every thread sets the same value
     if (!attr_set) {
       cudaFuncSetAttribute(topk_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kTcMaxKeys * (int)sizeof(uint32_t));
+                           3 * kTcMaxKeys * (int)sizeof(uint32_t));
       attr_set = true;
     }
-    const size_t smem = (size_t)(keys_per_cta > 0 ? keys_per_cta : 1) * sizeof(uint32_t);
-    topk_cluster_kernel<<<(unsigned)(d->num_sel * kTcCtas), kTcThreads, smem, as_stream(stream)>>>(a);
+    const int cap = (int)(keys_per_cta > 0 ? keys_per_cta : 1);
+    const size_t smem = 3 * (size_t)cap * sizeof(uint32_t);
+    topk_cluster_kernel<<<(unsigned)(d->num_sel * kTcCtas), kTcThreads, smem, as_stream(stream)>>>(a, cap);
     return after_launch("mskv_topk");
   }
   topk_kernel<<<d->num_sel, kTkThreads, 0, as_stream(stream)>>>(a);

@@ -11,7 +11,7 @@ import ctypes as C
 import math
 import weakref
 from dataclasses import dataclass
-from typing import Optional, Sequence
+from typing import Optional, Sequence, Tuple
 
 import numpy as np
 import torch
@@ -312,25 +312,50 @@ def score(q: torch.Tensor, k: RowsSpec, *, batch: int, kv_heads: int, max_tokens
     return out
 
 
+def blocked_layout(blocks: int, num_sel: int, rows_per_block: int, row_len: int) -> Tuple[int, int, int]:
+    """(sel_stride, row_block, block_stride) of a contiguous [blocks, num_sel, rows_per_block,
+    row_len] score tensor: row r of selection j starts at
+    j*sel_stride + (r // row_block)*block_stride + (r % row_block)*row_len."""
+    return rows_per_block * row_len, rows_per_block, num_sel * rows_per_block * row_len
+
+
 def topk(scores: torch.Tensor, *, top_k, recent: int = 0, len_: Optional[torch.Tensor] = None,
          len_scalar: Optional[int] = None, rows_per_sel: int = 1, sel_per_batch: int = 1,
          scale: float = 1.0, out: Optional[torch.Tensor] = None, counts: Optional[torch.Tensor] = None,
-         out_dtype: torch.dtype = torch.int32, stream: Optional[torch.cuda.Stream] = None):
+         out_dtype: torch.dtype = torch.int32, stream: Optional[torch.cuda.Stream] = None,
+         row_blocks: Optional[tuple] = None):
     """Sorted top-k ∪ recent-window indices per selection (mskv_topk).
 
     scores: fp32 [num_rows, >= T] with a common row stride (num_rows = num_sel*rows_per_sel).
     top_k: int, or int32 device tensor [B] (per sequence).
+    row_blocks: (blocks, num_sel, rows_per_block) for scores laid out as a contiguous
+    [blocks, num_sel, rows_per_block, T] tensor (per-head score rows all-gathered from the
+    ranks that hold the heads); selection j then sums its blocks*rows_per_block rows in
+    block-major order, i.e. in global head order.
     Returns (idx [num_sel, K_max + recent], counts int32 [num_sel]).
     """
     if scores.dtype != torch.float32 or scores.stride(-1) != 1:
         raise ValueError("scores must be fp32 with a contiguous token axis")
-    rows = scores.reshape(-1, scores.shape[-1]) if scores.is_contiguous() else scores
-    if rows.dim() != 2:
-        raise ValueError("scores must be 2-D or contiguous")
-    if rows.shape[0] % rows_per_sel:
-        raise ValueError("number of score rows must be a multiple of rows_per_sel")
-    num_sel = rows.shape[0] // rows_per_sel
+    sel_stride = block_stride = row_block = 0
+    if row_blocks is not None:
+        nblk, nsel_b, rpb = (int(x) for x in row_blocks)
+        if not scores.is_contiguous() or scores.numel() != nblk * nsel_b * rpb * scores.shape[-1]:
+            raise ValueError("row_blocks needs a contiguous [blocks, num_sel, rows_per_block, T] tensor")
+        rows = scores.reshape(-1, scores.shape[-1])
+        if rows_per_sel != nblk * rpb:
+            raise ValueError("rows_per_sel must equal blocks * rows_per_block")
+        num_sel = nsel_b
+        sel_stride, row_block, block_stride = blocked_layout(nblk, nsel_b, rpb, rows.shape[1])
+    else:
+        rows = scores.reshape(-1, scores.shape[-1]) if scores.is_contiguous() else scores
+        if rows.dim() != 2:
+            raise ValueError("scores must be 2-D or contiguous")
+        if rows.shape[0] % rows_per_sel:
+            raise ValueError("number of score rows must be a multiple of rows_per_sel")
+        num_sel = rows.shape[0] // rows_per_sel
     T = rows.shape[1] if len_scalar is None else int(len_scalar)
+    if T > rows.shape[1]:
+        raise ValueError("len_scalar exceeds the score rows")
     dev = scores.device
     if isinstance(top_k, torch.Tensor):
         if top_k.dtype != torch.int32 or not top_k.is_contiguous():
@@ -361,6 +386,7 @@ def topk(scores: torch.Tensor, *, top_k, recent: int = 0, len_: Optional[torch.T
     d.recent = int(recent)
     d.num_sel, d.rows_per_sel, d.sel_per_batch = num_sel, rows_per_sel, sel_per_batch
     d.out_bits = 64 if out.dtype == torch.int64 else 32
+    d.row_block, d.sel_stride, d.block_stride = row_block, sel_stride, block_stride
     check(lib().mskv_topk(C.byref(d), _stream_ptr(stream)))
     return out, counts
 

@@ -31,7 +31,7 @@ def test_ctypes_bindings_cover_the_header(built_lib):
     declared = set(_declared_functions())
     assert bound <= declared
     lib = _lib.lib()
-    assert lib.mskv_abi_version() == 1
+    assert lib.mskv_abi_version() == 2
     assert isinstance(_lib.launch_count(), int)
 
 

@@ -1,0 +1,105 @@
+"""Head-sharded shared selection: the host logic on gloo ranks (CPU, world sizes 2 and 4).
+
+Each rank computes the GQA-summed score rows of its own KV heads with the oracle, the rows are
+exchanged with mserve_b200.parallel.exchange_head_scores, and the blocked row layout that
+mserve_b200.parallel hands to the top-k kernel (ops.blocked_layout) is walked here the way the
+kernel walks it.  Every sequence must see its Hkv rows in global head order, bit for bit, and
+the oracle's selection over them must equal the unsharded selection.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import kv_oracle as ko
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(seed: int, B=3, Hq=16, Hkv=4, T=257, D=32):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, Hq, D)).astype(np.float32)
+    k = rng.standard_normal((B, Hkv, T, D)).astype(np.float32)
+    return q, k
+
+
+def _rows_of_selection(flat: np.ndarray, j: int, rows: int, layout, row_len: int) -> np.ndarray:
+    """Rows r = 0..rows-1 of selection j, addressed as mskv_topk addresses them."""
+    sel_stride, row_block, block_stride = layout
+    out = []
+    for r in range(rows):
+        off = j * sel_stride + (r // row_block) * block_stride + (r % row_block) * row_len
+        out.append(flat[off:off + row_len])
+    return np.stack(out)
+
+
+def _worker(rank, world, port, seed, top_k, recent):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from mserve_b200 import ops, parallel
+        q, k = _case(seed)
+        B, Hq, _ = q.shape
+        Hkv, T = k.shape[1], k.shape[2]
+        G = Hq // Hkv
+        full = ko.gqa_scores(q, k).astype(np.float32)                  # [B, Hkv, T], all heads
+        h0, h1 = parallel.head_shard(Hkv, world, rank)
+        Hl = h1 - h0
+        local = ko.gqa_scores(q[:, h0 * G:h1 * G], k[:, h0:h1]).astype(np.float32)
+        assert np.array_equal(local, full[:, h0:h1])                    # heads are independent
+        gathered = torch.empty(world, B, Hl, T)
+        parallel.exchange_head_scores(torch.from_numpy(np.ascontiguousarray(local)), gathered)
+        layout = ops.blocked_layout(world, B, Hl, T)
+        flat = gathered.numpy().reshape(-1)
+        for b in range(B):
+            rows = _rows_of_selection(flat, b, Hkv, layout, T)
+            assert np.array_equal(rows, full[b]), f"rank {rank}: rows of sequence {b} out of head order"
+        # the selection over the exchanged rows equals the unsharded one
+        regathered = np.stack([_rows_of_selection(flat, b, Hkv, layout, T) for b in range(B)]).reshape(B * Hkv, T)
+        sel_s, cnt_s = ko.select_topk_window(regathered, top_k=top_k, recent=recent, rows_per_sel=Hkv,
+                                             scale=np.float32(1.0 / Hq))
+        sel_f, cnt_f = ko.select_topk_window(full.reshape(B * Hkv, T), top_k=top_k, recent=recent,
+                                             rows_per_sel=Hkv, scale=np.float32(1.0 / Hq))
+        assert list(cnt_s) == list(cnt_f)
+        for a, b_ in zip(sel_s, sel_f):
+            assert np.array_equal(a, b_)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_exchange_matches_unsharded(world):
+    port = _free_port()
+    mp.start_processes(_worker, args=(world, port, 17 + world, 40, 16), nprocs=world, join=True,
+                       start_method="spawn")
+
+
+def test_head_shard_splits():
+    from mserve_b200 import parallel
+    assert [parallel.head_shard(8, 4, r) for r in range(4)] == [(0, 2), (2, 4), (4, 6), (6, 8)]
+    assert parallel.head_shard(8, 1, 0) == (0, 8)
+    with pytest.raises(ValueError):
+        parallel.head_shard(4, 8, 0)          # fewer heads than ranks
+    with pytest.raises(ValueError):
+        parallel.head_shard(8, 2, 2)          # rank out of range
+
+
+def test_blocked_layout_single_block_is_plain_rows():
+    from mserve_b200 import ops
+    # one block: row r of selection j at (j*R + r) * T -- the unsharded [B, Hkv, T] layout
+    sel_stride, row_block, block_stride = ops.blocked_layout(1, 5, 4, 100)
+    assert (sel_stride, row_block) == (400, 4)
+    for j in range(5):
+        for r in range(4):
+            assert j * sel_stride + (r // row_block) * block_stride + (r % row_block) * 100 == (j * 4 + r) * 100
