@@ -21,6 +21,7 @@ Decode step, per layer (``decode_layer``): GQA-summed fp32 scores from the HBM p
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 from typing import List, Optional, Sequence
 
@@ -47,19 +48,30 @@ class OffloadKV:
     num_layers, batch, q_heads, kv_heads, head_dim: model/batch geometry.
     capacity: tokens per sequence in the host store (and in the page table).
     top_k, recent: the selection per (sequence, KV head): top_k tokens of [0, L - recent)
-    plus the last `recent` tokens.
+    plus the last `recent` tokens.  top_k_ratio instead of top_k: ceil(top_k_ratio * L_b)
+    tokens for sequence b, following each sequence's length.
+    For KV heads sharded over GPUs, each rank builds its engine with its own heads (kv_heads =
+    its share, q_heads = the matching query heads); per-head selection needs no exchange.
     """
 
     def __init__(self, num_layers: int, batch: int, q_heads: int, kv_heads: int, head_dim: int, capacity: int, *,
-                 top_k: int, recent: int = 0, dtype: torch.dtype = torch.bfloat16, page_size: int = 16,
+                 top_k: int = 0, recent: int = 0, top_k_ratio: Optional[float] = None,
+                 dtype: torch.dtype = torch.bfloat16, page_size: int = 16,
                  device: Optional[torch.device] = None, host_alloc=None):
         if q_heads % kv_heads:
             raise ValueError("q_heads must be a multiple of kv_heads")
+        if top_k_ratio is not None and not 0.0 < top_k_ratio <= 1.0:
+            raise ValueError("top_k_ratio must lie in (0, 1]")
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.L, self.B, self.Hq, self.Hkv, self.D = num_layers, batch, q_heads, kv_heads, head_dim
         self.C, self.page_size, self.dtype = capacity, page_size, dtype
         self.top_k, self.recent = int(top_k), int(recent)
-        self.S = self.top_k + self.recent
+        self.top_k_ratio = top_k_ratio
+        # per-sequence k (host copy and device copy), refreshed by commit()
+        self.topk_h = np.zeros(batch, dtype=np.int64)
+        self.topk_dev = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        k_cap = math.ceil(top_k_ratio * capacity) if top_k_ratio is not None else self.top_k
+        self.S = k_cap + self.recent
         alloc = host_alloc or ops.host_empty
         self.host_k: List[torch.Tensor] = [alloc((batch, kv_heads, capacity, head_dim), dtype) for _ in range(num_layers)]
         self.host_v: List[torch.Tensor] = [alloc((batch, kv_heads, capacity, head_dim), dtype) for _ in range(num_layers)]
@@ -129,6 +141,9 @@ class OffloadKV:
         n_new, tok0, counts = self._pending
         self.len_h = self.len_h + n_new
         self.lens.copy_(torch.from_numpy(self.len_h.astype(np.int32)), non_blocking=False)
+        if self.top_k_ratio is not None:
+            self.topk_h = np.array([math.ceil(self.top_k_ratio * int(n)) for n in self.len_h], dtype=np.int64)
+            self.topk_dev.copy_(torch.from_numpy(self.topk_h.astype(np.int32)), non_blocking=False)
         # tok0/counts were read by kernels on the current stream; keep them alive until then.
         cur = torch.cuda.current_stream(self.device)
         tok0.record_stream(cur)
@@ -154,10 +169,17 @@ class OffloadKV:
         T = int(self.len_h.max(initial=0))
         keys = ops.paged_rows(self.pool_k[layer], None, self.page_table, len_=self.lens)
         ops.score(q, keys, batch=self.B, kv_heads=self.Hkv, max_tokens=T, out=bufs.scores, method=0)
-        ops.topk(bufs.scores.view(self.B * self.Hkv, self.C), top_k=self.top_k, recent=self.recent,
+        top_k, k_bound = self._top_k(0, self.B)
+        ops.topk(bufs.scores.view(self.B * self.Hkv, self.C), top_k=top_k, recent=self.recent,
                  len_=self.lens, len_scalar=T, rows_per_sel=1, sel_per_batch=self.Hkv,
-                 out=bufs.idx, counts=bufs.counts)
+                 out=bufs.idx, counts=bufs.counts, k_bound=k_bound)
         return bufs.idx, bufs.counts
+
+    def _top_k(self, b0: int, b1: int):
+        """(top_k argument, host bound) of sequences [b0, b1) for ops.topk."""
+        if self.top_k_ratio is None:
+            return self.top_k, None
+        return self.topk_dev[b0:b1], int(self.topk_h[b0:b1].max(initial=0))
 
     def gather(self, layer: int, idx: torch.Tensor, counts: torch.Tensor, bufs: Optional[DecodeBuffers] = None):
         """Selected K/V rows from the host store into HBM [B, Hkv, S, D]."""
@@ -194,8 +216,9 @@ class OffloadKV:
         def select():
             keys = ops.paged_rows(self.pool_k[layer], None, self.page_table[b0:b1], len_=lens)
             ops.score(q[b0:b1], keys, batch=nb, kv_heads=Hkv, max_tokens=T, out=scores, method=0)
-            ops.topk(scores.view(nb * Hkv, C), top_k=self.top_k, recent=self.recent, len_=lens, len_scalar=T,
-                     rows_per_sel=1, sel_per_batch=Hkv, out=idx, counts=counts)
+            top_k, k_bound = self._top_k(b0, b1)
+            ops.topk(scores.view(nb * Hkv, C), top_k=top_k, recent=self.recent, len_=lens, len_scalar=T,
+                     rows_per_sel=1, sel_per_batch=Hkv, out=idx, counts=counts, k_bound=k_bound)
 
         def gather():
             src = ops.strided_rows(self.host_k[layer][b0:b1], self.host_v[layer][b0:b1], len_=lens,

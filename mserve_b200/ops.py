@@ -323,11 +323,12 @@ def topk(scores: torch.Tensor, *, top_k, recent: int = 0, len_: Optional[torch.T
          len_scalar: Optional[int] = None, rows_per_sel: int = 1, sel_per_batch: int = 1,
          scale: float = 1.0, out: Optional[torch.Tensor] = None, counts: Optional[torch.Tensor] = None,
          out_dtype: torch.dtype = torch.int32, stream: Optional[torch.cuda.Stream] = None,
-         row_blocks: Optional[tuple] = None):
+         row_blocks: Optional[tuple] = None, k_bound: Optional[int] = None):
     """Sorted top-k ∪ recent-window indices per selection (mskv_topk).
 
     scores: fp32 [num_rows, >= T] with a common row stride (num_rows = num_sel*rows_per_sel).
-    top_k: int, or int32 device tensor [B] (per sequence).
+    top_k: int, or int32 device tensor [B] (per sequence); k_bound, when given, bounds every
+    top_k[b] (the caller knows it on the host: no device read, so the call can be captured).
     row_blocks: (blocks, num_sel, rows_per_block) for scores laid out as a contiguous
     [blocks, num_sel, rows_per_block, T] tensor (per-head score rows all-gathered from the
     ranks that hold the heads); selection j then sums its blocks*rows_per_block rows in
@@ -360,7 +361,10 @@ def topk(scores: torch.Tensor, *, top_k, recent: int = 0, len_: Optional[torch.T
     if isinstance(top_k, torch.Tensor):
         if top_k.dtype != torch.int32 or not top_k.is_contiguous():
             raise ValueError("per-sequence top_k must be contiguous int32")
-        k_max = int(top_k.max().item()) if top_k.numel() else 0
+        if k_bound is not None:
+            k_max = int(k_bound)
+        else:
+            k_max = int(top_k.max().item()) if top_k.numel() else 0
         k_ptr, k_scalar = top_k.data_ptr(), 0
     else:
         k_max, k_ptr, k_scalar = int(top_k), None, int(top_k)
