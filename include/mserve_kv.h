@@ -142,6 +142,9 @@ typedef struct mskv_gather_desc {
   int32_t batch;
   int32_t heads;
   int32_t num_selected;         /* rows per segment (upper bound when counts != NULL) */
+  int32_t max_ctas;             /* grid bound; 0: library default (bounded when either
+                                   side is host memory, the full grid otherwise)       */
+  int32_t pad_;
 } mskv_gather_desc;
 int mskv_gather(const mskv_gather_desc* d, void* stream);
 
@@ -162,7 +165,7 @@ typedef struct mskv_copy_desc {
   int32_t batch;
   int32_t heads;
   int32_t num_tokens;
-  int32_t pad_;
+  int32_t max_ctas;             /* grid bound; 0: library default, as mskv_gather     */
 } mskv_copy_desc;
 int mskv_copy_rows(const mskv_copy_desc* d, void* stream);
 

@@ -53,6 +53,7 @@ class GatherDesc(C.Structure):
         ("counts", _vp), ("cnt_stride_b", _i64), ("cnt_stride_h", _i64),
         ("row_bytes", _i64), ("status", _vp),
         ("index_bits", _i32), ("batch", _i32), ("heads", _i32), ("num_selected", _i32),
+        ("max_ctas", _i32), ("pad_", _i32),
     ]
 
 
@@ -60,7 +61,7 @@ class CopyDesc(C.Structure):
     _fields_ = [
         ("src", Rows), ("dst", Rows),
         ("counts", _vp), ("row_bytes", _i64), ("status", _vp),
-        ("batch", _i32), ("heads", _i32), ("num_tokens", _i32), ("pad_", _i32),
+        ("batch", _i32), ("heads", _i32), ("num_tokens", _i32), ("max_ctas", _i32),
     ]
 
 

@@ -34,6 +34,7 @@ struct MoveDev {
   int32_t tiles;            // ceil(rows_max / rows_per_cta)
   int32_t chunk_shift;      // log2(row_bytes / VEC) or -1
   int32_t zero_invalid;     // zero-fill destination rows whose source is invalid
+  int32_t work;             // tiles in all segments (segments x tiles)
 };
 
 template <int VEC>
@@ -42,75 +43,79 @@ __global__ void __launch_bounds__(kThreads) move_rows_kernel(const MoveDev a) {
   __shared__ int64_t s_src[kMaxRowsPerCta];
   __shared__ int64_t s_dst[kMaxRowsPerCta];
 
-  const int seg = blockIdx.x / a.tiles;
-  const int tile = blockIdx.x - seg * a.tiles;
-  const int b = seg / a.heads;
-  const int h = seg - b * a.heads;
-  int count = a.rows_max;
-  if (a.counts) {
-    count = a.counts[(int64_t)b * a.cnt_sb + (int64_t)h * a.cnt_sh];
-    if (count > a.rows_max) count = a.rows_max;
-  }
-  const int r0 = tile * a.rows_per_cta;
-  if (r0 >= count) return;  // uniform across the CTA
-  const int nrows = min(a.rows_per_cta, count - r0);
-
-  if (threadIdx.x < nrows) {
-    const int i = r0 + threadIdx.x;
-    uint32_t why = 0;
-    int64_t st;
-    if (a.idx) {
-      const int64_t o = (int64_t)b * a.idx_sb + (int64_t)h * a.idx_sh + i;
-      st = a.idx64 ? static_cast<const int64_t*>(a.idx)[o] : (int64_t) static_cast<const int32_t*>(a.idx)[o];
-    } else {
-      st = (a.src.tok0 ? a.src.tok0[b] : 0) + (int64_t)i;
-    }
-    const int64_t dt = (a.dst.tok0 ? a.dst.tok0[b] : 0) + (int64_t)i;
-    int64_t so = rows_offset(a.src, b, h, st, &why, MSKV_STATUS_INDEX_OOB);
-    const int64_t dof = rows_offset(a.dst, b, h, dt, &why, MSKV_STATUS_DST_OOB);
-    if (so < 0 && !a.zero_invalid) so = -1;
-    s_src[threadIdx.x] = so;
-    s_dst[threadIdx.x] = dof;
-    if (why && a.status) atomicOr(a.status, why);
-  }
-  __syncthreads();
-
   const int64_t chunks = a.row_bytes / VEC;
-  const int64_t total = (int64_t)nrows * chunks;
   const char* __restrict__ sk = a.src.base_k;
   const char* __restrict__ sv = a.src.base_v;
   char* __restrict__ dk = const_cast<char*>(a.dst.base_k);
   char* __restrict__ dv = const_cast<char*>(a.dst.base_v);
   const bool has_v = sv != nullptr;
 
-  for (int64_t base = threadIdx.x; base < total; base += (int64_t)kThreads * kUnroll) {
-    V rk[kUnroll], rv[kUnroll];
-    int64_t dofs[kUnroll];
+  // Grid-stride loop over the tiles: the grid may be smaller than the work (see launch_move).
+  for (int w = blockIdx.x; w < a.work; w += gridDim.x) {
+    const int seg = w / a.tiles;
+    const int tile = w - seg * a.tiles;
+    const int b = seg / a.heads;
+    const int h = seg - b * a.heads;
+    int count = a.rows_max;
+    if (a.counts) {
+      count = a.counts[(int64_t)b * a.cnt_sb + (int64_t)h * a.cnt_sh];
+      if (count > a.rows_max) count = a.rows_max;
+    }
+    const int r0 = tile * a.rows_per_cta;
+    if (r0 >= count) continue;  // uniform across the CTA
+    const int nrows = min(a.rows_per_cta, count - r0);
+
+    __syncthreads();  // the previous tile's readers of s_src / s_dst are done
+    if (threadIdx.x < nrows) {
+      const int i = r0 + threadIdx.x;
+      uint32_t why = 0;
+      int64_t st;
+      if (a.idx) {
+        const int64_t o = (int64_t)b * a.idx_sb + (int64_t)h * a.idx_sh + i;
+        st = a.idx64 ? static_cast<const int64_t*>(a.idx)[o] : (int64_t) static_cast<const int32_t*>(a.idx)[o];
+      } else {
+        st = (a.src.tok0 ? a.src.tok0[b] : 0) + (int64_t)i;
+      }
+      const int64_t dt = (a.dst.tok0 ? a.dst.tok0[b] : 0) + (int64_t)i;
+      int64_t so = rows_offset(a.src, b, h, st, &why, MSKV_STATUS_INDEX_OOB);
+      const int64_t dof = rows_offset(a.dst, b, h, dt, &why, MSKV_STATUS_DST_OOB);
+      if (so < 0 && !a.zero_invalid) so = -1;
+      s_src[threadIdx.x] = so;
+      s_dst[threadIdx.x] = dof;
+      if (why && a.status) atomicOr(a.status, why);
+    }
+    __syncthreads();
+
+    const int64_t total = (int64_t)nrows * chunks;
+    for (int64_t base = threadIdx.x; base < total; base += (int64_t)kThreads * kUnroll) {
+      V rk[kUnroll], rv[kUnroll];
+      int64_t dofs[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t item = base + (int64_t)u * kThreads;
-      dofs[u] = -1;
-      rk[u] = V{};
-      rv[u] = V{};
-      if (item < total) {
-        const int64_t r = a.chunk_shift >= 0 ? (item >> a.chunk_shift) : (item / chunks);
-        const int64_t c = item - r * chunks;
-        const int64_t so = s_src[r];
-        const int64_t dof = s_dst[r];
-        if (dof >= 0 && (so >= 0 || a.zero_invalid)) {
-          dofs[u] = dof + c * VEC;
-          if (so >= 0) {
-            rk[u] = *reinterpret_cast<const V*>(sk + so + c * VEC);
-            if (has_v) rv[u] = *reinterpret_cast<const V*>(sv + so + c * VEC);
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t item = base + (int64_t)u * kThreads;
+        dofs[u] = -1;
+        rk[u] = V{};
+        rv[u] = V{};
+        if (item < total) {
+          const int64_t r = a.chunk_shift >= 0 ? (item >> a.chunk_shift) : (item / chunks);
+          const int64_t c = item - r * chunks;
+          const int64_t so = s_src[r];
+          const int64_t dof = s_dst[r];
+          if (dof >= 0 && (so >= 0 || a.zero_invalid)) {
+            dofs[u] = dof + c * VEC;
+            if (so >= 0) {
+              rk[u] = *reinterpret_cast<const V*>(sk + so + c * VEC);
+              if (has_v) rv[u] = *reinterpret_cast<const V*>(sv + so + c * VEC);
+            }
           }
         }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      if (dofs[u] >= 0) {
-        *reinterpret_cast<V*>(dk + dofs[u]) = rk[u];
-        if (has_v) *reinterpret_cast<V*>(dv + dofs[u]) = rv[u];
+      for (int u = 0; u < kUnroll; ++u) {
+        if (dofs[u] >= 0) {
+          *reinterpret_cast<V*>(dk + dofs[u]) = rk[u];
+          if (has_v) *reinterpret_cast<V*>(dv + dofs[u]) = rv[u];
+        }
       }
     }
   }
@@ -135,7 +140,14 @@ static int pick_vec(const MoveDev& m) {
   return 1;
 }
 
-static int launch_move(MoveDev m, cudaStream_t stream, const char* what) {
+// CTAs of a move that reads or writes host memory.  Every row load a CTA issues stays in
+// flight for the PCIe round trip, and loads queued behind the host link also hold up the HBM
+// traffic of kernels running beside the move.  The link needs only bandwidth x latency in
+// flight (tens to hundreds of KB), so a bounded grid (about 32 KB per CTA per round) keeps it
+// busy without flooding the memory system; HBM-only moves use the full grid.
+constexpr int kHostLinkCtas = 32;
+
+static int launch_move(MoveDev m, cudaStream_t stream, const char* what, int max_ctas) {
   const int64_t segs = (int64_t)m.batch * m.heads;
   if (segs == 0 || m.rows_max == 0) return MSKV_OK;
   const int vec = pick_vec(m);
@@ -151,8 +163,10 @@ static int launch_move(MoveDev m, cudaStream_t stream, const char* what) {
     while ((1LL << s) < chunks) ++s;
     m.chunk_shift = s;
   }
-  const int64_t blocks = segs * m.tiles;
-  if (blocks > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "%s: grid too large", what);
+  const int64_t work = segs * m.tiles;
+  if (work > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "%s: grid too large", what);
+  m.work = (int)work;
+  const int64_t blocks = max_ctas > 0 && max_ctas < work ? max_ctas : work;
   switch (vec) {
     case 16: move_rows_kernel<16><<<(unsigned)blocks, kThreads, 0, stream>>>(m); break;
     case 8: move_rows_kernel<8><<<(unsigned)blocks, kThreads, 0, stream>>>(m); break;
@@ -163,20 +177,32 @@ static int launch_move(MoveDev m, cudaStream_t stream, const char* what) {
   return after_launch(what);
 }
 
-// Resolves the device-accessible address of a (possibly host) base pointer.
-static int resolve(const void* p, const void** out, const char* what) {
+// Resolves the device-accessible address of a (possibly host) base pointer; *host is set
+// when the memory lives on the host side of the link.
+static int resolve(const void* p, const void** out, const char* what, bool* host = nullptr) {
   if (!p) { *out = nullptr; return MSKV_OK; }
   void* d = nullptr;
   int rc = mskv_device_view(p, &d);
   if (rc != MSKV_OK) return fail(rc, "%s: %s", what, mskv_last_error());
+  if (host && d != p) *host = true;
+  if (host && d == p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) == cudaSuccess && at.type == cudaMemoryTypeHost) *host = true;
+    cudaGetLastError();
+  }
   *out = d;
   return MSKV_OK;
 }
 
-static int resolve_rows(mskv_rows& r, const char* side) {
-  int rc = resolve(r.base_k, &r.base_k, side);
+static int resolve_rows(mskv_rows& r, const char* side, bool* host) {
+  int rc = resolve(r.base_k, &r.base_k, side, host);
   if (rc) return rc;
-  return resolve(r.base_v, &r.base_v, side);
+  return resolve(r.base_v, &r.base_v, side, host);
+}
+
+static int grid_cap(int requested, bool host) {
+  if (requested > 0) return requested;
+  return host ? kHostLinkCtas : 0;
 }
 
 }  // namespace mskv
@@ -208,9 +234,10 @@ int mskv_uva_gather(const void* k_in, const void* v_in, const int64_t* indices,
   dst.base_k = k_out; dst.base_v = v_out;
   dst.stride_t = row; dst.stride_h = num_selected * row; dst.stride_b = num_heads * num_selected * row;
   dst.len_scalar = num_selected;
-  int rc = resolve_rows(src, "mskv_uva_gather k_in/v_in");
+  bool host = false;
+  int rc = resolve_rows(src, "mskv_uva_gather k_in/v_in", &host);
   if (rc) return rc;
-  rc = resolve_rows(dst, "mskv_uva_gather k_out/v_out");
+  rc = resolve_rows(dst, "mskv_uva_gather k_out/v_out", &host);
   if (rc) return rc;
   const void* idx_dev = nullptr;
   rc = resolve(indices, &idx_dev, "mskv_uva_gather indices");
@@ -220,7 +247,7 @@ int mskv_uva_gather(const void* k_in, const void* v_in, const int64_t* indices,
   m.idx = idx_dev; m.idx64 = 1; m.idx_sb = 0; m.idx_sh = 0;
   m.row_bytes = row; m.status = status; m.batch = (int)batch_size; m.heads = (int)num_heads;
   m.rows_max = (int)num_selected; m.zero_invalid = 1;
-  return launch_move(m, as_stream(stream), "mskv_uva_gather");
+  return launch_move(m, as_stream(stream), "mskv_uva_gather", grid_cap(0, host));
 }
 
 int mskv_gather(const mskv_gather_desc* d, void* stream) {
@@ -236,15 +263,17 @@ int mskv_gather(const mskv_gather_desc* d, void* stream) {
   if (rc) return rc;
   rc = check_rows(dst, "mskv_gather dst", need_v);
   if (rc) return rc;
-  if ((rc = resolve_rows(src, "mskv_gather src"))) return rc;
-  if ((rc = resolve_rows(dst, "mskv_gather dst"))) return rc;
+  if (d->max_ctas < 0) return fail(MSKV_ERR_ARG, "mskv_gather: negative max_ctas");
+  bool host = false;
+  if ((rc = resolve_rows(src, "mskv_gather src", &host))) return rc;
+  if ((rc = resolve_rows(dst, "mskv_gather dst", &host))) return rc;
   MoveDev m{};
   m.src = to_dev(src); m.dst = to_dev(dst);
   m.idx = d->indices; m.idx64 = d->index_bits == 64; m.idx_sb = d->idx_stride_b; m.idx_sh = d->idx_stride_h;
   m.counts = d->counts; m.cnt_sb = d->cnt_stride_b; m.cnt_sh = d->cnt_stride_h;
   m.row_bytes = d->row_bytes; m.status = d->status; m.batch = d->batch; m.heads = d->heads;
   m.rows_max = d->num_selected; m.zero_invalid = 1;
-  return launch_move(m, as_stream(stream), "mskv_gather");
+  return launch_move(m, as_stream(stream), "mskv_gather", grid_cap(d->max_ctas, host));
 }
 
 int mskv_copy_rows(const mskv_copy_desc* d, void* stream) {
@@ -258,15 +287,17 @@ int mskv_copy_rows(const mskv_copy_desc* d, void* stream) {
   if (rc) return rc;
   rc = check_rows(dst, "mskv_copy_rows dst", need_v);
   if (rc) return rc;
-  if ((rc = resolve_rows(src, "mskv_copy_rows src"))) return rc;
-  if ((rc = resolve_rows(dst, "mskv_copy_rows dst"))) return rc;
+  if (d->max_ctas < 0) return fail(MSKV_ERR_ARG, "mskv_copy_rows: negative max_ctas");
+  bool host = false;
+  if ((rc = resolve_rows(src, "mskv_copy_rows src", &host))) return rc;
+  if ((rc = resolve_rows(dst, "mskv_copy_rows dst", &host))) return rc;
   MoveDev m{};
   m.src = to_dev(src); m.dst = to_dev(dst);
   m.idx = nullptr;
   m.counts = d->counts; m.cnt_sb = 1; m.cnt_sh = 0;
   m.row_bytes = d->row_bytes; m.status = d->status; m.batch = d->batch; m.heads = d->heads;
   m.rows_max = d->num_tokens; m.zero_invalid = 0;
-  return launch_move(m, as_stream(stream), "mskv_copy_rows");
+  return launch_move(m, as_stream(stream), "mskv_copy_rows", grid_cap(d->max_ctas, host));
 }
 
 }  // extern "C"

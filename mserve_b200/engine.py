@@ -87,8 +87,13 @@ class OffloadKV:
         self.len_h = np.zeros(batch, dtype=np.int64)
         self.lens = torch.zeros(batch, dtype=torch.int32, device=self.device)
         self.ring_start = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        # Per-sequence split of a selection (refreshed by commit): the top-k part holds k'_b =
+        # min(k_b, n_b) rows, n_b = max(L_b - recent, 0), and the recent window the w_b = L_b - n_b
+        # tokens [n_b, L_b) at output rows [k'_b, k'_b + w_b).  [n_b, k'_b, w_b] per sequence.
+        self.split = torch.zeros(3, batch, dtype=torch.int32, device=self.device)
         self._pending = None
         self._bufs: Optional[DecodeBuffers] = None
+        self._sel2 = None
 
     # ------------------------------------------------------------------ append
     def reserve(self, n_new: Sequence[int]) -> None:
@@ -144,6 +149,10 @@ class OffloadKV:
         if self.top_k_ratio is not None:
             self.topk_h = np.array([math.ceil(self.top_k_ratio * int(n)) for n in self.len_h], dtype=np.int64)
             self.topk_dev.copy_(torch.from_numpy(self.topk_h.astype(np.int32)), non_blocking=False)
+        n = np.maximum(self.len_h - self.recent, 0)
+        k = self.topk_h if self.top_k_ratio is not None else np.full(self.B, self.top_k, dtype=np.int64)
+        split = np.stack([n, np.minimum(k, n), self.len_h - n]).astype(np.int32)
+        self.split.copy_(torch.from_numpy(split), non_blocking=False)
         # tok0/counts were read by kernels on the current stream; keep them alive until then.
         cur = torch.cuda.current_stream(self.device)
         tok0.record_stream(cur)
@@ -203,15 +212,46 @@ class OffloadKV:
         return self.attend(q, counts, bufs)
 
     # ------------------------------------------------------------------ pipelined decode step
-    def _chunk_ops(self, layer: int, q: torch.Tensor, b0: int, b1: int, bufs: DecodeBuffers, T: int):
-        """Kernels of one layer for sequences [b0, b1): (select, gather, attend) closures."""
+    def _host_rows(self, layer: int, b0: int, b1: int, tok0: Optional[torch.Tensor] = None) -> ops.RowsSpec:
+        return ops.strided_rows(self.host_k[layer][b0:b1], self.host_v[layer][b0:b1], len_=self.lens[b0:b1],
+                                ring_start=self.ring_start[b0:b1], ring_cap=self.C, tok0=tok0,
+                                device=self.device)
+
+    def _sel_rows(self, parity: int, bufs: DecodeBuffers):
+        """Selected-row buffers (k_sel, v_sel) of set `parity`: layers alternate between two
+        sets in the pipelined step, so one layer's window rows can land while the previous
+        layer's attention still reads its own rows."""
+        if parity == 0:
+            return bufs.k_sel, bufs.v_sel
+        if self._sel2 is None:
+            self._sel2 = (torch.empty_like(bufs.k_sel), torch.empty_like(bufs.v_sel))
+        return self._sel2
+
+    def _window_rows(self, layer: int, k_sel: torch.Tensor, v_sel: torch.Tensor) -> None:
+        """The recent-window rows of every sequence (tokens [n_b, L_b) -> rows [k'_b, k'_b + w_b)):
+        they are selected whatever the scores, so they can move before the query exists."""
+        if self.recent <= 0:
+            return
+        n0, kp, w = self.split[0], self.split[1], self.split[2]
+        dst = ops.strided_rows(k_sel, v_sel, tok0=kp, device=self.device)
+        ops.copy_rows(self._host_rows(layer, 0, self.B, tok0=n0), dst, batch=self.B, num_tokens=self.recent,
+                      counts=w, device=self.device)
+
+    def _chunk_ops(self, layer: int, q: torch.Tensor, b0: int, b1: int, bufs: DecodeBuffers, T: int,
+                   sel_rows=None, window_done: bool = False):
+        """Kernels of one layer for sequences [b0, b1): (select, gather, attend) closures.
+
+        window_done: the window rows are already in sel_rows (see _window_rows), so the gather
+        moves only the top-k part of each selection."""
         Hkv, C = self.Hkv, self.C
         nb = b1 - b0
         lens = self.lens[b0:b1]
         scores = bufs.scores[b0:b1]
         idx = bufs.idx[b0 * Hkv:b1 * Hkv]
         counts = bufs.counts[b0 * Hkv:b1 * Hkv]
-        k_sel, v_sel = bufs.k_sel[b0:b1], bufs.v_sel[b0:b1]
+        k_all, v_all = sel_rows if sel_rows is not None else (bufs.k_sel, bufs.v_sel)
+        k_sel, v_sel = k_all[b0:b1], v_all[b0:b1]
+        gcounts = self.split[1][b0:b1] if window_done and self.recent > 0 else counts
 
         def select():
             keys = ops.paged_rows(self.pool_k[layer], None, self.page_table[b0:b1], len_=lens)
@@ -221,9 +261,8 @@ class OffloadKV:
                      rows_per_sel=1, sel_per_batch=Hkv, out=idx, counts=counts, k_bound=k_bound)
 
         def gather():
-            src = ops.strided_rows(self.host_k[layer][b0:b1], self.host_v[layer][b0:b1], len_=lens,
-                                   ring_start=self.ring_start[b0:b1], ring_cap=C, device=self.device)
-            ops.gather(src, idx.view(nb, Hkv, -1), k_sel, v_sel, batch=nb, counts=counts.view(nb, Hkv))
+            ops.gather(self._host_rows(layer, b0, b1), idx.view(nb, Hkv, -1), k_sel, v_sel, batch=nb,
+                       counts=gcounts.view(nb, -1))
 
         def attend(out):
             ops.sparse_attention(q[b0:b1].unsqueeze(2), k_sel, v_sel, counts=counts.view(nb, Hkv), out=out[b0:b1])
@@ -233,25 +272,33 @@ class OffloadKV:
     def decode_step(self, q_all: torch.Tensor, out_all: torch.Tensor, chunks: int = 4, streams=None) -> None:
         """All layers of one decode step, pipelined over sequence chunks.
 
-        q_all: [L, B, Hq, D]; out_all: [L, B, Hq, 1, D].  Within a layer, chunk c's scores and
+        q_all: [L, B, Hq, D]; out_all: [L, B, Hq, 1, D]; chunks: a number of equal chunks or
+        the list of chunk sizes (sequences).  Within a layer, chunk c's scores and
         selection run on the caller's stream, its gather on a second stream and its attention
         on a third, so the selection of chunk c+1 and the attention of chunk c-1 execute while
         chunk c's rows cross PCIe.  Layer l+1 starts only after layer l's attention (the model
         dependency).  The side streams fork from and join back into the caller's stream, so
-        the call can be captured in a CUDA graph.  Outputs are bit-identical to decode_layer.
+        the call can be captured in a CUDA graph.  The recent-window rows of layer l+1 (known
+        before its query) are copied while layer l finishes, into the second of two alternating
+        selected-row buffer sets.  Outputs are bit-identical to decode_layer.
         """
         bufs = self.buffers()
         T = int(self.len_h.max(initial=0))
         cur = torch.cuda.current_stream(self.device)
         s_gat, s_att = streams or self._side_streams()
-        bounds = np.linspace(0, self.B, min(chunks, self.B) + 1).astype(int)
+        bounds = self.chunk_bounds(chunks)
+        sel_rows = [self._sel_rows(0, bufs), self._sel_rows(1, bufs)]
         start = torch.cuda.Event()
         start.record(cur)
         s_gat.wait_event(start)
         s_att.wait_event(start)
+        with torch.cuda.stream(s_gat):
+            self._window_rows(0, *sel_rows[0])
         for layer in range(self.L):
             sel_ev, gat_ev = [], []
-            parts = [self._chunk_ops(layer, q_all[layer], int(bounds[c]), int(bounds[c + 1]), bufs, T)
+            rows = sel_rows[layer % 2]
+            parts = [self._chunk_ops(layer, q_all[layer], int(bounds[c]), int(bounds[c + 1]), bufs, T,
+                                     sel_rows=rows, window_done=True)
                      for c in range(len(bounds) - 1)]
             for select, _, _ in parts:
                 select()
@@ -265,6 +312,11 @@ class OffloadKV:
                     g = torch.cuda.Event()
                     g.record(s_gat)
                     gat_ev.append(g)
+                # The next layer's window rows cross the link while this layer's last attention
+                # and the next layer's first selection run.  Their buffer set was last read by
+                # the attention of layer - 1, which finished before this layer's selections.
+                if layer + 1 < self.L:
+                    self._window_rows(layer + 1, *sel_rows[(layer + 1) % 2])
             with torch.cuda.stream(s_att):
                 for (_, _, attend), g in zip(parts, gat_ev):
                     s_att.wait_event(g)
@@ -275,6 +327,15 @@ class OffloadKV:
         end = torch.cuda.Event()
         end.record(s_gat)
         cur.wait_event(end)
+
+    def chunk_bounds(self, chunks) -> np.ndarray:
+        """Sequence boundaries of the chunks: `chunks` equal parts, or explicit chunk sizes."""
+        if isinstance(chunks, (int, np.integer)):
+            return np.linspace(0, self.B, min(int(chunks), self.B) + 1).astype(int)
+        sizes = [int(c) for c in chunks]
+        if not sizes or min(sizes) <= 0 or sum(sizes) != self.B:
+            raise ValueError(f"chunk sizes {sizes} must be positive and sum to the batch {self.B}")
+        return np.concatenate([[0], np.cumsum(sizes)]).astype(int)
 
     def _side_streams(self):
         if getattr(self, "_streams", None) is None:

@@ -202,8 +202,10 @@ def paged_rows(k_pool: torch.Tensor, v_pool: Optional[torch.Tensor], page_table:
 # ---------------------------------------------------------------------------------------
 def gather(src: RowsSpec, indices: torch.Tensor, out_k: torch.Tensor, out_v: Optional[torch.Tensor] = None,
            *, batch: int, counts: Optional[torch.Tensor] = None, status: bool = True,
-           stream: Optional[torch.cuda.Stream] = None) -> None:
+           stream: Optional[torch.cuda.Stream] = None, max_ctas: int = 0) -> None:
     """out[b,h,s,:] = src[b,h,indices[...,s],:] for s < count(b,h) (mskv_gather).
+
+    max_ctas: grid bound (0: the library's default, bounded for host memory).
 
     indices: int32/int64, shape [S] (shared by all segments), [B, S] (shared by the heads of
     a sequence) or [B, H, S] (one list per segment), contiguous, on the output's device.
@@ -248,13 +250,16 @@ def gather(src: RowsSpec, indices: torch.Tensor, out_k: torch.Tensor, out_v: Opt
     d.status = status_word(out_k.device).data_ptr() if status else None
     d.index_bits = 64 if indices.dtype == torch.int64 else 32
     d.batch, d.heads, d.num_selected = batch, heads, S
+    d.max_ctas = int(max_ctas)
     check(lib().mskv_gather(C.byref(d), _stream_ptr(stream)))
 
 
 def copy_rows(src: RowsSpec, dst: RowsSpec, *, batch: int, num_tokens: int,
               counts: Optional[torch.Tensor] = None, device: Optional[torch.device] = None,
-              status: bool = True, stream: Optional[torch.cuda.Stream] = None) -> None:
-    """Row i < count[b] of every (b,h): dst[b,h,dst.tok0[b]+i] = src[b,h,src.tok0[b]+i] (mskv_copy_rows)."""
+              status: bool = True, stream: Optional[torch.cuda.Stream] = None, max_ctas: int = 0) -> None:
+    """Row i < count[b] of every (b,h): dst[b,h,dst.tok0[b]+i] = src[b,h,src.tok0[b]+i] (mskv_copy_rows).
+
+    max_ctas: grid bound (0: the library's default, bounded for host memory)."""
     if src.row_bytes != dst.row_bytes or src.heads != dst.heads:
         raise ValueError("source and destination rows differ in size or head count")
     dev = device or torch.device("cuda", torch.cuda.current_device())
@@ -267,6 +272,7 @@ def copy_rows(src: RowsSpec, dst: RowsSpec, *, batch: int, num_tokens: int,
     d.row_bytes = src.row_bytes
     d.status = status_word(dev).data_ptr() if status else None
     d.batch, d.heads, d.num_tokens = batch, src.heads, num_tokens
+    d.max_ctas = int(max_ctas)
     check(lib().mskv_copy_rows(C.byref(d), _stream_ptr(stream)))
 
 
