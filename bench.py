@@ -175,15 +175,12 @@ def measured_peaks():
     return {}
 
 
-def ncu_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu summary (None if absent)."""
-    p = ROOT / "profiles" / "ncu_traffic.json"
-    if not p.exists():
-        return None
-    try:
-        return json.loads(p.read_text()).get(kernel)
-    except ValueError:
-        return None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per decode layer of this workload, from
+# one ncu --set full capture of each kernel (profiles/gather_decode_qwen7b.txt,
+# profiles/select_decode_qwen7b.txt).  The gather's algorithmic bytes cross PCIe, not DRAM: its
+# 1,114,112 sysmem sectors x 32 B equal the 35.65 MB gathered.
+NCU_DRAM_BYTES = {"gather": 290304 + 28160, "select": 138077440 + 2138880}
+NCU_SYSMEM_BYTES = {"gather": (1048576 + 65536) * 32}
 
 
 # ------------------------------------------------------------------------------------- workload
@@ -355,20 +352,6 @@ def run_mserve(args, world, rank, local):
     key_bytes_layer = eng.B * eng.Hkv * wl["seq_len"] * eng.D * 2
     stream = torch.cuda.current_stream(dev)
 
-    def step(ev=None):
-        for layer in range(L):
-            if ev is not None:
-                ev[layer][0].record(stream)
-            idx, cnt = eng.select(layer, q[layer], bufs)
-            if ev is not None:
-                ev[layer][1].record(stream)
-            eng.gather(layer, idx, cnt, bufs)
-            if ev is not None:
-                ev[layer][2].record(stream)
-            eng.attend(q[layer], cnt, bufs)
-            if ev is not None:
-                ev[layer][3].record(stream)
-
     # The product path: the whole decode step (all layers, chunk-pipelined over three streams)
     # captured once as a CUDA graph and replayed.
     out_all = torch.empty((L,) + tuple(bufs.out.shape), dtype=bufs.out.dtype, device=dev)
@@ -397,18 +380,40 @@ def run_mserve(args, world, rank, local):
     value = total_bytes / t_max / 1e9
     ms_step = t_max / args.steps * 1e3
 
-    # Per-kernel durations for the roofline: the same kernels run layer by layer (no overlap)
-    # with CUDA events around each phase, right after the timed region.
-    bd_steps = min(args.steps, 5)
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(L)] for _ in range(bd_steps)]
-    step()
-    for s_ in range(bd_steps):
-        step(evs[s_])
-    torch.cuda.synchronize(dev)
-    sel_ms = statistics.mean(e[l][0].elapsed_time(e[l][1]) for e in evs for l in range(L))
-    gat_ms = statistics.mean(e[l][1].elapsed_time(e[l][2]) for e in evs for l in range(L))
-    att_ms = statistics.mean(e[l][2].elapsed_time(e[l][3]) for e in evs for l in range(L))
-    serial_ms_step = statistics.mean(e[0][0].elapsed_time(e[L - 1][3]) for e in evs)
+    # Per-kernel durations for the rooflines: each phase of every layer -- scores + top-k, the
+    # gather, the attention -- captured as its own CUDA graph and replayed back to back, timed
+    # with CUDA events on the launching stream (no other phase runs beside it).
+    def phase_graph(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()                                    # warm-up: workspaces are allocated here
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side, capture_error_mode="relaxed"):
+            fn()
+        return g
+
+    def per_layer_ms(g, reps=3):
+        g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / (reps * L)
+
+    g_sel = phase_graph(lambda: [eng.select(layer, q[layer], bufs) for layer in range(L)])
+    sel_ms = per_layer_ms(g_sel)
+    g_gat = phase_graph(lambda: [eng.gather(layer, bufs.idx, bufs.counts, bufs) for layer in range(L)])
+    gat_ms = per_layer_ms(g_gat)
+    g_att = phase_graph(lambda: [eng.attend(q[layer], bufs.counts, bufs) for layer in range(L)])
+    att_ms = per_layer_ms(g_att)
+    del g_sel, g_gat, g_att
+    serial_ms_step = L * (sel_ms + gat_ms + att_ms)
+    ops.check_status(dev, "bench phase timing")
 
     # end to end through the public API: q from pinned host each step, outputs back to host
     e2e = None
@@ -464,14 +469,17 @@ def run_mserve(args, world, rank, local):
     roofline = {"bound": "host_link", "kernel": "move_rows_kernel (mskv_gather)", "achieved": gather_gbs,
                 "peak": peaks["h2d"], "unit": "GB/s", "frac": gather_gbs / peaks["h2d"],
                 "peak_source": "pinned cudaMemcpyAsync H2D, 256 MiB, best of 5, measured in this run",
-                "algorithmic_bytes_per_launch": gb_layer, "traffic": ncu_traffic("gather")}
+                "algorithmic_bytes_per_launch": gb_layer, "traffic": NCU_DRAM_BYTES["gather"],
+                "link_traffic": NCU_SYSMEM_BYTES["gather"],
+                "timing": "gather kernels of all layers replayed as one CUDA graph, CUDA events"}
     hbm_peak = peaks_json.get("hbm_gbs", 6650.0)
     score_gbs = key_bytes_layer / (sel_ms * 1e-3) / 1e9
     roofline_select = {"bound": "hbm", "kernel": "score_stream_kernel + topk_cluster_kernel", "achieved": score_gbs,
                        "peak": hbm_peak, "unit": "GB/s", "frac": score_gbs / hbm_peak,
                        "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks_json
                        else "fallback 6650 GB/s", "algorithmic_bytes_per_launch": key_bytes_layer,
-                       "traffic": ncu_traffic("score")}
+                       "traffic": NCU_DRAM_BYTES["select"],
+                       "timing": "score + top-k kernels of all layers replayed as one CUDA graph, CUDA events"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -484,7 +492,8 @@ def run_mserve(args, world, rank, local):
                        "l2": "inputs larger than L2: 3.76 GB of HBM keys + 1 GB of host KV read per step"},
             "roofline": roofline, "roofline_select": roofline_select,
             "breakdown_ms_per_layer": {"score_topk": sel_ms, "gather": gat_ms, "attention": att_ms,
-                                       "note": "same kernels run layer by layer without overlap, after the timed region"},
+                                       "note": "each phase of all layers replayed alone as a CUDA graph after the timed region; "
+                                               "the attention then reads its rows from L2"},
             "serial_ms_per_step": serial_ms_step, "chunks": args.chunks,
             "pcie_peak_gbs": peaks, "gather_frac_of_h2d_peak_whole_step": value / world / peaks["h2d"],
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),

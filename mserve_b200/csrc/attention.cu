@@ -294,16 +294,18 @@ __global__ void __launch_bounds__(kAtThreads) attn_mma_kernel(const AttnDev a) {
       mma16816<BF16>(oacc[n + 1], pa[k2], vb[2], vb[3]);
     }
   }
-  // warp partial -> shared memory (the warp's own K rows are free now): O as fp32 [16][D]
+  // warp partial -> shared memory (the warp's own K rows are free now): O as fp32 [16][OS],
+  // row stride OS = D + 8 floats so each half-warp's 8-byte stores hit 32 distinct banks;
+  // 16 * OS * 4 bytes == 32 * ROWP, exactly the warp's rows
+  constexpr int OS = D + 8;
+  static_assert(16 * OS * 4 <= 32 * ROWP, "warp partial must fit in the warp's K rows");
   __syncwarp();
-  float* so = reinterpret_cast<float*>(sK + wrow0 * ROWP);   // 16*D*4 bytes <= 32*ROWP
+  float* so = reinterpret_cast<float*>(sK + wrow0 * ROWP);
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     const int col = n * 8 + 2 * tig;
-    so[g * D + col] = oacc[n][0];
-    so[g * D + col + 1] = oacc[n][1];
-    so[(g + 8) * D + col] = oacc[n][2];
-    so[(g + 8) * D + col + 1] = oacc[n][3];
+    *reinterpret_cast<float2*>(so + g * OS + col) = make_float2(oacc[n][0], oacc[n][1]);
+    *reinterpret_cast<float2*>(so + (g + 8) * OS + col) = make_float2(oacc[n][2], oacc[n][3]);
   }
   if (tig == 0) {
     s_m[warp][g] = wrows > 0 ? m_lo : -INFINITY;
@@ -326,7 +328,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_mma_kernel(const AttnDev a) {
       if (s_m[w][r] == -INFINITY) continue;
       const float f = __expf(s_m[w][r] - M);
       L += s_l[w][r] * f;
-      o += reinterpret_cast<const float*>(sK + w * 32 * ROWP)[r * D + d] * f;
+      o += reinterpret_cast<const float*>(sK + w * 32 * ROWP)[r * OS + d] * f;
     }
     wp[(int64_t)r * (D + 2) + d] = o;
     if (d == 0) {
