@@ -144,8 +144,12 @@ class ClockSampler:
 
 
 def pcie_peaks(device, nbytes=256 << 20, reps=5):
-    """Pinned cudaMemcpyAsync H2D / D2H peak of this GPU's host link (GB/s, best of reps)."""
-    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    """Pinned cudaMemcpyAsync H2D / D2H peak of this GPU's host link (GB/s, best of reps), from
+    host memory on the GPU's NUMA node.  Under torchrun every rank measures at the same time,
+    so the figure is the per-GPU peak with all links busy."""
+    from mserve_b200 import topology
+    with topology.local_placement(device):
+        h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     g = torch.empty(nbytes, dtype=torch.uint8, device=device)
     out = {}
     for name in ("h2d", "d2h"):
@@ -347,6 +351,9 @@ def run_mserve(args, world, rank, local):
     L = wl["layers"]
     eng, q = build_engine(wl, dev, seed=1000 + rank)
     bufs = eng.buffers()
+    from mserve_b200 import topology
+    numa_node = topology.numa_node(dev)
+    barrier(world)
     peaks = pcie_peaks(dev)
     gb_layer = gathered_bytes(eng)
     key_bytes_layer = eng.B * eng.Hkv * wl["seq_len"] * eng.D * 2
@@ -495,7 +502,9 @@ def run_mserve(args, world, rank, local):
                                        "note": "each phase of all layers replayed alone as a CUDA graph after the timed region; "
                                                "the attention then reads its rows from L2"},
             "serial_ms_per_step": serial_ms_step, "chunks": args.chunks,
-            "pcie_peak_gbs": peaks, "gather_frac_of_h2d_peak_whole_step": value / world / peaks["h2d"],
+            "pcie_peak_gbs": peaks,
+            "host_placement": {"numa_node": numa_node, "local_cpus": len(eng.host_cpus),
+                               "note": "host store allocated on the GPU's local CPUs (0: placement left to the system)"}, "gather_frac_of_h2d_peak_whole_step": value / world / peaks["h2d"],
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
             "clocks": clk.summary(),
         }

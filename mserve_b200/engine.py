@@ -21,6 +21,7 @@ Decode step, per layer (``decode_layer``): GQA-summed fp32 scores from the HBM p
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 from typing import List, Optional, Sequence
@@ -28,7 +29,7 @@ from typing import List, Optional, Sequence
 import numpy as np
 import torch
 
-from . import ops
+from . import ops, topology
 
 
 @dataclass
@@ -57,7 +58,7 @@ class OffloadKV:
     def __init__(self, num_layers: int, batch: int, q_heads: int, kv_heads: int, head_dim: int, capacity: int, *,
                  top_k: int = 0, recent: int = 0, top_k_ratio: Optional[float] = None,
                  dtype: torch.dtype = torch.bfloat16, page_size: int = 16,
-                 device: Optional[torch.device] = None, host_alloc=None):
+                 device: Optional[torch.device] = None, host_alloc=None, numa_local: bool = True):
         if q_heads % kv_heads:
             raise ValueError("q_heads must be a multiple of kv_heads")
         if top_k_ratio is not None and not 0.0 < top_k_ratio <= 1.0:
@@ -73,8 +74,14 @@ class OffloadKV:
         k_cap = math.ceil(top_k_ratio * capacity) if top_k_ratio is not None else self.top_k
         self.S = k_cap + self.recent
         alloc = host_alloc or ops.host_empty
-        self.host_k: List[torch.Tensor] = [alloc((batch, kv_heads, capacity, head_dim), dtype) for _ in range(num_layers)]
-        self.host_v: List[torch.Tensor] = [alloc((batch, kv_heads, capacity, head_dim), dtype) for _ in range(num_layers)]
+        # The host store goes on the NUMA node of this GPU's PCIe link (numa_local).
+        placement = topology.local_placement(self.device) if numa_local else contextlib.nullcontext(set())
+        with placement as cpus:
+            self.host_cpus = cpus
+            self.host_k: List[torch.Tensor] = [alloc((batch, kv_heads, capacity, head_dim), dtype)
+                                               for _ in range(num_layers)]
+            self.host_v: List[torch.Tensor] = [alloc((batch, kv_heads, capacity, head_dim), dtype)
+                                               for _ in range(num_layers)]
         self.max_pages = (capacity + page_size - 1) // page_size
         self.num_pages = batch * self.max_pages
         self.pool_k: List[torch.Tensor] = [

@@ -73,3 +73,9 @@ def test_host_side_errors_without_gpu(built_lib):
     k = torch.zeros(1, 2, 10, 8, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="pinned"):
         cuda_uva.uva_gather(k, k, torch.tensor([0]), 1, 2, 10, 8)
+
+
+def test_cpulist_parsing():
+    from mserve_b200 import topology
+    assert topology.parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert topology.parse_cpulist("") == set()
