@@ -214,9 +214,10 @@ int mskv_score(const mskv_score_desc* d, void* stream);
  * (ties broken toward the lower token index, NaN ranks highest), and appends the window
  * [n, L).  The output row idx[j*out_stride ...] is sorted ascending and holds
  * count = k + (L - n) entries; counts[j] receives it (may be NULL).  Scores of the
- * candidates only are read.  When len != NULL, len_scalar must bound every len[b] (it sizes
- * the kernel: up to 131072 candidates, a cluster of 8 CTAs per selection holds the keys in
- * shared memory; beyond that one CTA per selection re-reads them from L2). */
+ * candidates only are read.  When len != NULL, len_scalar bounds every len[b] (larger values
+ * are clamped to it) and sizes the kernel: up to 49152 candidates one 1024-thread CTA per
+ * selection keeps the keys in shared memory; up to 131072 a cluster of 8 CTAs does; beyond
+ * that one CTA per selection re-reads them from L2. */
 typedef struct mskv_topk_desc {
   const float* scores;
   int64_t scores_stride;

@@ -55,6 +55,40 @@ __device__ __forceinline__ uint32_t key_at(const TopkDev& a, const float* row0, 
   return order_key(s * a.scale);
 }
 
+// Keys [0, n) of a selection into shared memory, NL independent loads in flight per thread
+// (the same fp32 sum, in row order, as key_at).  With hist != NULL every key also adds one to
+// hist[key >> hist_shift].
+template <int NL>
+__device__ __forceinline__ void load_keys(const TopkDev& a, const float* row0, int64_t lo, int n,
+                                          uint32_t* s_keys, int tid, int nthreads, uint32_t* hist = nullptr,
+                                          int hist_shift = 0) {
+  for (int base = tid; base < n; base += NL * nthreads) {
+    float v[NL];
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = base + u * nthreads;
+      v[u] = i < n ? row0[lo + i] : 0.f;
+    }
+    for (int r = 1; r < a.rows_per_sel; ++r) {
+      const float* rr = row0 + (int64_t)(r / a.row_block) * a.block_stride + (int64_t)(r % a.row_block) * a.ss;
+#pragma unroll
+      for (int u = 0; u < NL; ++u) {
+        const int i = base + u * nthreads;
+        if (i < n) v[u] += rr[lo + i];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = base + u * nthreads;
+      if (i < n) {
+        const uint32_t key = order_key(v[u] * a.scale);
+        s_keys[i] = key;
+        if (hist) atomicAdd(&hist[key >> hist_shift], 1u);
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void put(const TopkDev& a, int64_t j, int64_t pos, int64_t tok) {
   if (a.out64) reinterpret_cast<int64_t*>(a.out)[j * a.os + pos] = tok;
   else reinterpret_cast<int32_t*>(a.out)[j * a.os + pos] = (int32_t)tok;
@@ -93,7 +127,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_kernel(const TopkDev a) {
 
   const int64_t j = blockIdx.x;
   const int b = (int)(j / a.sel_per_batch);
-  const int64_t L = a.len ? (int64_t)a.len[b] : (int64_t)a.len_scalar;
+  const int64_t L = a.len ? min((int64_t)a.len[b], (int64_t)a.len_scalar) : (int64_t)a.len_scalar;
   const int64_t n = L > a.recent ? L - a.recent : 0;  // candidates [0, n)
   int64_t K = a.topk ? (int64_t)a.topk[b] : (int64_t)a.k_scalar;
   if (K < 0) K = 0;
@@ -187,6 +221,187 @@ __global__ void __launch_bounds__(kTkThreads) topk_kernel(const TopkDev a) {
 }
 
 // ---------------------------------------------------------------------------------------
+// Shared-memory path (up to kSmMaxKeys candidates): one 1024-thread CTA per selection keeps
+// every candidate key in shared memory, so no step needs more than __syncthreads.
+//
+// Digits of 12, 12 and 8 bits: the first pass histograms every key into 4096 bins (plain
+// shared atomics; a 12-bit digit of an fp32 key spans an eighth of a binade, so real scores
+// spread over many bins); the second and third passes only compare keys against the prefix
+// and count the few that still match.  Each digit search is a block-wide suffix scan over the
+// histogram.  The ordered compaction is the warp-ballot one of the cluster path.
+constexpr int kSmThreads = 1024;
+constexpr int kSmWarps = kSmThreads / 32;
+constexpr int kSmMaxKeys = 48 * 1024;  // a multiple of 4: the buffer holds whole 4-key units
+constexpr int kSmBins = 4096;
+
+__device__ __forceinline__ uint32_t lanemask_lt_sm() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Finds the bin holding the krem-th largest key of the histogram (bins ordered by value);
+// sets *prefix |= bin << shift and *krem to the rank within that bin.  Every thread calls it.
+__device__ __forceinline__ void sm_digit_search(const uint32_t* hist, int nbins, int shift, uint32_t* s_wsuf,
+                                                uint32_t* s_prefix, uint32_t* s_krem, uint32_t& prefix,
+                                                uint32_t& krem) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // thread t owns bins [4t, 4t+4)
+  uint32_t c[4] = {0, 0, 0, 0};
+  if (4 * tid < nbins) {
+    const uint4 v = reinterpret_cast<const uint4*>(hist)[tid];
+    c[0] = v.x; c[1] = v.y; c[2] = v.z; c[3] = v.w;
+  }
+  const uint32_t own = c[0] + c[1] + c[2] + c[3];
+  uint32_t suf = own;  // inclusive suffix over the lanes of the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+    if (lane + o < 32) suf += v;
+  }
+  if (lane == 0) s_wsuf[warp] = suf;  // warp total
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t wt = s_wsuf[lane];
+    uint32_t ws = wt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_down_sync(0xffffffffu, ws, o);
+      if (lane + o < 32) ws += v;
+    }
+    __syncwarp();
+    s_wsuf[lane] = ws - wt;  // total of the warps above
+  }
+  __syncthreads();
+  uint32_t cum = s_wsuf[warp] + (suf - own);  // keys in bins above this thread's bins
+#pragma unroll
+  for (int i = 3; i >= 0; --i) {
+    if (cum < krem && cum + c[i] >= krem) {
+      *s_prefix = prefix | ((uint32_t)(4 * tid + i) << shift);
+      *s_krem = krem - cum;
+    }
+    cum += c[i];
+  }
+  __syncthreads();
+  prefix = *s_prefix;
+  krem = *s_krem;
+}
+
+__global__ void __launch_bounds__(kSmThreads) topk_smem_kernel(const TopkDev a) {
+  extern __shared__ __align__(16) uint32_t s_keys[];   // n keys, padded to a multiple of 4
+  __shared__ __align__(16) uint32_t s_hist[kSmBins];
+  __shared__ uint32_t s_wsuf[kSmWarps];
+  __shared__ uint64_t s_wcnt[kSmWarps];
+  __shared__ uint32_t s_prefix, s_krem;
+
+  const int64_t j = blockIdx.x;
+  const int b = (int)(j / a.sel_per_batch);
+  // len_scalar bounds every len[b] (it sized the key buffer): a larger len[b] is clamped
+  const int64_t L = a.len ? min((int64_t)a.len[b], (int64_t)a.len_scalar) : (int64_t)a.len_scalar;
+  const int n = (int)(L > a.recent ? L - a.recent : 0);
+  int64_t K = a.topk ? (int64_t)a.topk[b] : (int64_t)a.k_scalar;
+  if (K < 0) K = 0;
+  if (K > n) K = n;
+  const int64_t w = L - n;
+  const float* row0 = a.scores + j * a.sel_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint4* keys4 = reinterpret_cast<const uint4*>(s_keys);
+  const int n4 = (n + 3) >> 2;  // 4-key units; the last may be partial (its tail is masked)
+
+  if (K > 0 && K < n) {
+    for (int i = tid; i < kSmBins; i += kSmThreads) s_hist[i] = 0;
+    __syncthreads();
+    // keys into shared memory; digit 0 (bits 31..20) histogrammed on the way
+    load_keys<16>(a, row0, 0, n, s_keys, tid, kSmThreads, s_hist, 20);
+    __syncthreads();
+    uint32_t prefix = 0, krem = (uint32_t)K;
+    sm_digit_search(s_hist, kSmBins, 20, s_wsuf, &s_prefix, &s_krem, prefix, krem);
+    // digit 1: bits 19..8 of the keys whose top 12 bits match
+    for (int i = tid; i < kSmBins; i += kSmThreads) s_hist[i] = 0;
+    __syncthreads();
+    for (int u = tid; u < n4; u += kSmThreads) {
+      const uint4 kv = keys4[u];
+      const uint32_t k4[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (4 * u + e < n && (k4[e] >> 20) == (prefix >> 20)) atomicAdd(&s_hist[(k4[e] >> 8) & 0xfffu], 1u);
+    }
+    __syncthreads();
+    sm_digit_search(s_hist, kSmBins, 8, s_wsuf, &s_prefix, &s_krem, prefix, krem);
+    // digit 2: bits 7..0 of the keys whose top 24 bits match
+    for (int i = tid; i < 256; i += kSmThreads) s_hist[i] = 0;
+    __syncthreads();
+    for (int u = tid; u < n4; u += kSmThreads) {
+      const uint4 kv = keys4[u];
+      const uint32_t k4[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (4 * u + e < n && (k4[e] >> 8) == (prefix >> 8)) atomicAdd(&s_hist[k4[e] & 0xffu], 1u);
+    }
+    __syncthreads();
+    sm_digit_search(s_hist, 256, 0, s_wsuf, &s_prefix, &s_krem, prefix, krem);
+
+    // Ordered compaction through bitmaps.  Word q covers keys [32q, 32q+32), bit i = key 32q+i:
+    // G_q marks keys above the threshold key, E_q keys equal to it (one ballot pair per word).
+    // A block scan of (#G, #E) per word gives every word its output position and how many of
+    // the equal keys before it were kept; its thread then writes only its selected keys.
+    const int nw = (n + 31) >> 5;                 // <= kSmMaxKeys / 32 = 1536 words
+    uint32_t* s_g = s_hist;                       // the histogram is free now
+    uint32_t* s_e = s_hist + kSmMaxKeys / 32;
+    __syncthreads();                              // the last digit search read s_hist
+    for (int q = warp; q < nw; q += kSmWarps) {
+      const int i = 32 * q + lane;
+      const uint32_t key = i < n ? s_keys[i] : 0u;
+      const uint32_t gm = __ballot_sync(0xffffffffu, i < n && key > prefix);
+      const uint32_t em = __ballot_sync(0xffffffffu, i < n && key == prefix);
+      if (lane == 0) { s_g[q] = gm; s_e[q] = em; }
+    }
+    __syncthreads();
+    // thread t owns words [t*WPT, t*WPT + WPT)
+    const int WPT = (nw + kSmThreads - 1) / kSmThreads;   // 1 or 2
+    const int q0 = min(tid * WPT, nw), q1 = min(q0 + WPT, nw);
+    uint64_t own = 0;
+    for (int q = q0; q < q1; ++q) own += ((uint64_t)__popc(s_g[q]) << 32) | (uint64_t)__popc(s_e[q]);
+    uint64_t inc = own;                            // inclusive scan over the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    if (lane == 31) s_wcnt[warp] = inc;
+    __syncthreads();
+    uint64_t before = lane < warp ? s_wcnt[lane] : 0;   // totals of the warps below
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
+    before += inc - own;
+    uint32_t gtb = (uint32_t)(before >> 32), eqb = (uint32_t)(before & 0xffffffffu);
+    for (int q = q0; q < q1; ++q) {
+      const uint32_t gm = s_g[q], em = s_e[q];
+      // keep the first (krem - eqb) equal keys, in token order
+      uint32_t keep = 0, rest = em;
+      for (uint32_t r = eqb; r < krem && rest; ++r) {
+        const uint32_t low = rest & (0u - rest);
+        keep |= low;
+        rest ^= low;
+      }
+      uint32_t sel = gm | keep;
+      int64_t pos = (int64_t)gtb + min(eqb, krem);
+      while (sel) {
+        const int bit = __ffs(sel) - 1;
+        put(a, j, pos++, 32 * q + bit);
+        sel &= sel - 1;
+      }
+      gtb += __popc(gm);
+      eqb += __popc(em);
+    }
+  } else if (K == n) {
+    for (int t = tid; t < n; t += kSmThreads) put(a, j, t, t);
+  }
+  for (int64_t i = tid; i < w; i += kSmThreads) put(a, j, K + i, n + i);
+  if (a.counts && tid == 0) a.counts[j] = (int32_t)(K + w);
+}
+
+// ---------------------------------------------------------------------------------------
 // Cluster path: 8 CTAs (one thread-block cluster) per selection.
 //
 // CTA r of the cluster owns the r-th eighth of the candidates and keeps their keys in shared
@@ -242,7 +457,8 @@ __global__ void __cluster_dims__(kTcCtas, 1, 1) __launch_bounds__(kTcThreads)
   const int rank = (int)cluster.block_rank();
   const int64_t j = blockIdx.x / kTcCtas;
   const int b = (int)(j / a.sel_per_batch);
-  const int64_t L = a.len ? (int64_t)a.len[b] : (int64_t)a.len_scalar;
+  // len_scalar bounds every len[b] (it sized the key buffers): a larger len[b] is clamped
+  const int64_t L = a.len ? min((int64_t)a.len[b], (int64_t)a.len_scalar) : (int64_t)a.len_scalar;
   const int64_t n = L > a.recent ? L - a.recent : 0;
   int64_t K = a.topk ? (int64_t)a.topk[b] : (int64_t)a.k_scalar;
   if (K < 0) K = 0;
@@ -259,7 +475,7 @@ __global__ void __cluster_dims__(kTcCtas, 1, 1) __launch_bounds__(kTcThreads)
     for (int i = tid; i < 4 * 256; i += kTcThreads) (&s_hist[0][0])[i] = 0;
     if (tid == 0) { s_n1 = 0; s_n2 = 0; }
     __syncthreads();
-    for (int i = tid; i < m; i += kTcThreads) s_keys[i] = key_at(a, row0, lo + i);
+    load_keys<8>(a, row0, lo, m, s_keys, tid, kTcThreads);
     // first digit's histogram: each thread reads back the keys it stored itself
     for (int base = 0; base < m; base += kTcThreads) {
       const int i = base + tid;
@@ -395,6 +611,17 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
   a.block_stride = d->block_stride;
   // len_scalar bounds every len[b]; it sizes the per-CTA key buffer of the cluster path.
   const int64_t n_max = d->len_scalar > d->recent ? (int64_t)d->len_scalar - d->recent : 0;
+  if (n_max <= kSmMaxKeys) {
+    static bool sm_attr_set = false;  // benign race: every thread sets the same value
+    if (!sm_attr_set) {
+      cudaFuncSetAttribute(topk_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kSmMaxKeys * (int)sizeof(uint32_t));
+      sm_attr_set = true;
+    }
+    const size_t smem = (size_t)((n_max + 3) / 4 * 4 + (n_max == 0 ? 4 : 0)) * sizeof(uint32_t);  // whole 4-key units
+    topk_smem_kernel<<<(unsigned)d->num_sel, kSmThreads, smem, as_stream(stream)>>>(a);
+    return after_launch("mskv_topk");
+  }
   const int64_t keys_per_cta = (n_max + kTcCtas - 1) / kTcCtas;
   if (keys_per_cta <= kTcMaxKeys && (int64_t)d->num_sel * kTcCtas <= 0x7fffffffLL) {
     static bool attr_set = false;  // benign race: every thread sets the same value

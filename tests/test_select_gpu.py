@@ -169,3 +169,36 @@ def test_scores_strided_rows(built_lib):
         ops.score(q.cuda(), ops.strided_rows(k, None), batch=B, kv_heads=Hkv, max_tokens=T, out=out)
         ref = ko.gqa_scores(q.float().numpy(), k.float().cpu().numpy())
         _assert_scores_close(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("T", [40000, 100000, 140000])   # shared-memory CTA, 8-CTA cluster, L2 re-read
+def test_topk_paths_ties_nan_ragged(built_lib, T):
+    """Each top-k path with quantised (tie-heavy) scores, NaN, ragged lengths and per-sequence k."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(T)
+    B, Hk = 2, 2
+    rows = (torch.randn(B * Hk, T, generator=g) * 4).round() * 0.25
+    rows[1, 17] = float("nan")
+    lens = torch.tensor([T, T // 2 + 3], dtype=torch.int32)
+    topk_b = torch.tensor([T // 8, 1000], dtype=torch.int32)
+    got, cnt = ops.topk(rows.cuda(), top_k=topk_b.cuda(), recent=128, len_=lens.cuda(), sel_per_batch=Hk)
+    ref, rcnt = ko.select_topk_window(rows.numpy(), top_k=topk_b.numpy(), recent=128, lens=lens.numpy(),
+                                      sel_per_batch=Hk)
+    got, cnt = got.cpu().numpy(), cnt.cpu().numpy()
+    np.testing.assert_array_equal(cnt, rcnt)
+    for j in range(B * Hk):
+        np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
+
+
+def test_topk_len_above_len_scalar_is_clamped(built_lib):
+    """len[b] beyond len_scalar (which sizes the kernel) is treated as len_scalar."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(5)
+    rows = torch.randn(2, 5000, generator=g)
+    lens = torch.tensor([5000, 3000], dtype=torch.int32)
+    got, cnt = ops.topk(rows.cuda(), top_k=100, recent=8, len_=lens.cuda(), len_scalar=2000)
+    ref, rcnt = ko.select_topk_window(rows.numpy(), top_k=100, recent=8, lens=[2000, 2000])
+    got, cnt = got.cpu().numpy(), cnt.cpu().numpy()
+    np.testing.assert_array_equal(cnt, rcnt)
+    for j in range(2):
+        np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
