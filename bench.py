@@ -401,7 +401,7 @@ def run_mserve(args, world, rank, local):
             fn()
         return g
 
-    def per_layer_ms(g, reps=3):
+    def per_layer_ms(g, reps=max(3, 84 // L)):
         g.replay()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -481,7 +481,7 @@ def run_mserve(args, world, rank, local):
                 "timing": "gather kernels of all layers replayed as one CUDA graph, CUDA events"}
     hbm_peak = peaks_json.get("hbm_gbs", 6650.0)
     score_gbs = key_bytes_layer / (sel_ms * 1e-3) / 1e9
-    roofline_select = {"bound": "hbm", "kernel": "score_stream_kernel + topk_cluster_kernel", "achieved": score_gbs,
+    roofline_select = {"bound": "hbm", "kernel": "score_stream_kernel + topk_smem_kernel", "achieved": score_gbs,
                        "peak": hbm_peak, "unit": "GB/s", "frac": score_gbs / hbm_peak,
                        "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks_json
                        else "fallback 6650 GB/s", "algorithmic_bytes_per_launch": key_bytes_layer,
