@@ -34,6 +34,7 @@ struct ScoreDev {
   int64_t slices_per_seg;
   int64_t total_slices;
   int64_t slices_per_warp;
+  int32_t page_shift;       // log2(page_size) when it is a power of two, else -1
 };
 
 template <typename T> struct Cvt;
@@ -249,22 +250,49 @@ struct SliceRef {
   bool ok;    // this lane group has rows and their page is mapped
 };
 
+// A warp's position in its run of slices: segment (b, h) and slice index within it.  The
+// segment fields are updated incrementally, so no slice needs an integer division.
+struct SliceCursor {
+  int64_t seg, sis, len;
+  int b, h;
+};
+
+__device__ __forceinline__ void cursor_init(const ScoreDev& a, SliceCursor& c, int64_t s) {
+  c.seg = s / a.slices_per_seg;
+  c.sis = s - c.seg * a.slices_per_seg;
+  c.b = (int)(c.seg / a.kv_heads);
+  c.h = (int)(c.seg - (int64_t)c.b * a.kv_heads);
+  c.len = rows_len(a.k, c.b);
+}
+
+__device__ __forceinline__ void cursor_next(const ScoreDev& a, SliceCursor& c) {
+  if (++c.sis == a.slices_per_seg) {
+    c.sis = 0;
+    ++c.seg;
+    if (++c.h == a.kv_heads) {
+      c.h = 0;
+      ++c.b;
+      if (c.b < a.batch) c.len = rows_len(a.k, c.b);
+    }
+  }
+}
+
 template <int D, bool PAGED>
-__device__ __forceinline__ SliceRef locate_slice(const ScoreDev& a, int64_t seg, int64_t slice_in_seg, int grp) {
+__device__ __forceinline__ SliceRef locate_slice(const ScoreDev& a, const SliceCursor& c, int grp) {
   constexpr int RPW = 8 * (32 / (D / 8));
   SliceRef r;
-  r.seg = seg;
-  r.b = (int)(seg / a.kv_heads);
-  r.h = (int)(seg - (int64_t)r.b * a.kv_heads);
-  r.len = rows_len(a.k, r.b);
-  const int64_t t_slice = slice_in_seg * RPW;
+  r.seg = c.seg;
+  r.b = c.b;
+  r.h = c.h;
+  r.len = c.len;
+  const int64_t t_slice = c.sis * RPW;
   r.live = t_slice < r.len;
   r.t0 = t_slice + grp * 8;
   r.ok = r.t0 < r.len;
   r.off0 = 0;
   if (r.ok) {
     if constexpr (PAGED) {
-      const int64_t pidx = r.t0 / a.k.page_size;
+      const int64_t pidx = a.page_shift >= 0 ? (r.t0 >> a.page_shift) : r.t0 / a.k.page_size;
       const int32_t page = a.k.page_table[(int64_t)r.b * a.k.pt_stride + pidx];
       r.ok = page >= 0 && page < a.k.num_pages;
       r.off0 = (int64_t)page * a.k.sp + (int64_t)r.h * a.k.sh + (r.t0 - pidx * a.k.page_size) * a.k.st;
@@ -340,14 +368,8 @@ __global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) 
   const int64_t s_end = min(s_begin + a.slices_per_warp, a.total_slices);
   if (s_begin >= s_end) return;
 
-  int64_t seg = s_begin / a.slices_per_seg;
-  int64_t sis = s_begin - seg * a.slices_per_seg;
-  auto advance = [&]() {
-    if (++sis == a.slices_per_seg) {
-      sis = 0;
-      ++seg;
-    }
-  };
+  SliceCursor cur_pos;
+  cursor_init(a, cur_pos, s_begin);
   float2 qs[4];
   int64_t q_seg = -1;
   auto score = [&](const SliceRef& r, const uint4 (&raw)[8]) {
@@ -362,22 +384,22 @@ __global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) 
   };
 
   uint4 bufA[8], bufB[8];
-  SliceRef cur = locate_slice<D, PAGED>(a, seg, sis, grp);
+  SliceRef cur = locate_slice<D, PAGED>(a, cur_pos, grp);
   issue_rows(a, cur, gl, bufA);
   for (int64_t s = s_begin; s < s_end; s += 2) {
     SliceRef nxt;
     const bool has1 = s + 1 < s_end;
     if (has1) {
-      advance();
-      nxt = locate_slice<D, PAGED>(a, seg, sis, grp);
+      cursor_next(a, cur_pos);
+      nxt = locate_slice<D, PAGED>(a, cur_pos, grp);
       issue_rows(a, nxt, gl, bufB);
     }
     score(cur, bufA);
     if (!has1) break;
     const bool has2 = s + 2 < s_end;
     if (has2) {
-      advance();
-      cur = locate_slice<D, PAGED>(a, seg, sis, grp);
+      cursor_next(a, cur_pos);
+      cur = locate_slice<D, PAGED>(a, cur_pos, grp);
       issue_rows(a, cur, gl, bufA);
     }
     score(nxt, bufB);
@@ -522,6 +544,12 @@ extern "C" int mskv_score(const mskv_score_desc* d, void* stream) {
   a.batch = d->batch; a.q_heads = d->q_heads; a.kv_heads = d->kv_heads; a.head_dim = d->head_dim;
   a.method = d->method;
   const bool paged = d->k.page_table != nullptr;
+  a.page_shift = -1;
+  if (paged && d->k.page_size > 0 && (d->k.page_size & (d->k.page_size - 1)) == 0) {
+    int sh = 0;
+    while ((1 << sh) < d->k.page_size) ++sh;
+    a.page_shift = sh;
+  }
   // The fast path needs 16-byte aligned rows/queries and, when paged, groups of up to 16
   // consecutive rows that never straddle a page.
   uint64_t al = (uint64_t)(uintptr_t)d->k.base_k | (uint64_t)d->k.stride_h | (uint64_t)d->k.stride_t;
