@@ -304,10 +304,16 @@ __device__ __forceinline__ SliceRef locate_slice(const ScoreDev& a, const SliceC
 }
 
 __device__ __forceinline__ void issue_rows(const ScoreDev& a, const SliceRef& r, int gl, uint4 (&raw)[8]) {
+  const char* p = a.k.base_k + r.off0 + gl * 16;
+  if (r.ok && r.t0 + 8 <= r.len) {          // a whole group: no per-row checks
+#pragma unroll
+    for (int j = 0; j < 8; ++j) raw[j] = ldg_stream(p + (int64_t)j * a.k.st);
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     raw[j] = make_uint4(0, 0, 0, 0);
-    if (r.ok && r.t0 + j < r.len) raw[j] = ldg_stream(a.k.base_k + r.off0 + (int64_t)j * a.k.st + gl * 16);
+    if (r.ok && r.t0 + j < r.len) raw[j] = ldg_stream(p + (int64_t)j * a.k.st);
   }
 }
 
