@@ -281,8 +281,9 @@ class OffloadKV:
 
         q_all: [L, B, Hq, D]; out_all: [L, B, Hq, 1, D]; chunks: a number of equal chunks or
         the list of chunk sizes (sequences).  Within a layer, chunk c's scores and
-        selection run on the caller's stream, its gather on a second stream and its attention
-        on a third, so the selection of chunk c+1 and the attention of chunk c-1 execute while
+        selection run on the caller's stream, its gather on one of two gather streams
+        (alternating, so consecutive gathers overlap at their boundaries) and its attention on
+        a fourth, so the selection of chunk c+1 and the attention of chunk c-1 execute while
         chunk c's rows cross PCIe.  Layer l+1 starts only after layer l's attention (the model
         dependency).  The side streams fork from and join back into the caller's stream, so
         the call can be captured in a CUDA graph.  The recent-window rows of layer l+1 (known
@@ -292,61 +293,84 @@ class OffloadKV:
         bufs = self.buffers()
         T = int(self.len_h.max(initial=0))
         cur = torch.cuda.current_stream(self.device)
-        s_gat, s_att = streams or self._side_streams()
+        s_g0, s_g1, s_att = streams or self._side_streams()
+        gat_streams = (s_g0, s_g1)
         bounds = self.chunk_bounds(chunks)
+        n_chunks = len(bounds) - 1
+        s_win = gat_streams[(n_chunks - 1) % 2]     # the stream of each layer's last gather
         sel_rows = [self._sel_rows(0, bufs), self._sel_rows(1, bufs)]
         start = torch.cuda.Event()
         start.record(cur)
-        s_gat.wait_event(start)
-        s_att.wait_event(start)
-        with torch.cuda.stream(s_gat):
+        for st in (s_g0, s_g1, s_att):
+            st.wait_event(start)
+        win_ev = torch.cuda.Event()
+        with torch.cuda.stream(s_win):
             self._window_rows(0, *sel_rows[0])
+            win_ev.record(s_win)
         for layer in range(self.L):
             sel_ev, gat_ev = [], []
             rows = sel_rows[layer % 2]
             parts = [self._chunk_ops(layer, q_all[layer], int(bounds[c]), int(bounds[c + 1]), bufs, T,
                                      sel_rows=rows, window_done=True)
-                     for c in range(len(bounds) - 1)]
+                     for c in range(n_chunks)]
             for select, _, _ in parts:
                 select()
                 e = torch.cuda.Event()
                 e.record(cur)
                 sel_ev.append(e)
-            with torch.cuda.stream(s_gat):
-                for (_, gather, _), e in zip(parts, sel_ev):
-                    s_gat.wait_event(e)
+            # Chunk c's gather runs on gather stream c % 2, so the tail of one chunk's gather
+            # overlaps the start of the next (the link stays busy across kernel boundaries).
+            for c, ((_, gather, _), e) in enumerate(zip(parts, sel_ev)):
+                st = gat_streams[c % 2]
+                with torch.cuda.stream(st):
+                    st.wait_event(e)
                     gather()
                     g = torch.cuda.Event()
-                    g.record(s_gat)
+                    g.record(st)
                     gat_ev.append(g)
+            this_win = win_ev
+            if layer + 1 < self.L:
                 # The next layer's window rows cross the link while this layer's last attention
                 # and the next layer's first selection run.  Their buffer set was last read by
                 # the attention of layer - 1, which finished before this layer's selections.
-                if layer + 1 < self.L:
+                win_ev = torch.cuda.Event()
+                with torch.cuda.stream(s_win):
                     self._window_rows(layer + 1, *sel_rows[(layer + 1) % 2])
+                    win_ev.record(s_win)
             with torch.cuda.stream(s_att):
+                s_att.wait_event(this_win)      # this layer's window rows are in place
                 for (_, _, attend), g in zip(parts, gat_ev):
                     s_att.wait_event(g)
                     attend(out_all[layer])
                 done = torch.cuda.Event()
                 done.record(s_att)
             cur.wait_event(done)                # the next layer's query needs this layer's output
-        end = torch.cuda.Event()
-        end.record(s_gat)
-        cur.wait_event(end)
+        for st in (s_g0, s_g1):
+            end = torch.cuda.Event()
+            end.record(st)
+            cur.wait_event(end)
 
     def chunk_bounds(self, chunks) -> np.ndarray:
-        """Sequence boundaries of the chunks: `chunks` equal parts, or explicit chunk sizes."""
+        """Sequence boundaries of the chunks: explicit chunk sizes, or a number of chunks.
+
+        For a number n the first chunk holds one sequence -- its selection is the only one on
+        the critical path of a layer, so the link starts as early as possible -- and the other
+        B - 1 sequences are split as evenly as possible into n - 1 chunks."""
         if isinstance(chunks, (int, np.integer)):
-            return np.linspace(0, self.B, min(int(chunks), self.B) + 1).astype(int)
+            n = max(1, min(int(chunks), self.B))
+            if n == 1:
+                return np.array([0, self.B])
+            rest = np.linspace(1, self.B, n).astype(int)      # n - 1 near-equal parts of [1, B)
+            return np.concatenate([[0], rest]).astype(int)
         sizes = [int(c) for c in chunks]
         if not sizes or min(sizes) <= 0 or sum(sizes) != self.B:
             raise ValueError(f"chunk sizes {sizes} must be positive and sum to the batch {self.B}")
         return np.concatenate([[0], np.cumsum(sizes)]).astype(int)
 
     def _side_streams(self):
+        """(gather stream 0, gather stream 1, attention stream)."""
         if getattr(self, "_streams", None) is None:
-            self._streams = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+            self._streams = tuple(torch.cuda.Stream(self.device) for _ in range(3))
         return self._streams
 
     def capture_decode_step(self, q_all: torch.Tensor, out_all: torch.Tensor, chunks: int = 4):
