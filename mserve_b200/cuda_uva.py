@@ -76,7 +76,13 @@ def uva_gather(k_in: torch.Tensor, v_in: torch.Tensor, indices: torch.Tensor, ba
         lo, hi = int(idx64.min()), int(idx64.max())
         if lo < 0 or hi >= T:
             raise RuntimeError(f"indices out of range [0, {T}): min {lo}, max {hi}")
-        idx = idx64.contiguous().to(dev, non_blocking=False)
+        # Asynchronous H2D of the index list from page-locked memory (a pinned staging copy
+        # for pageable input; torch keeps the pinned block until the copy has run), so the
+        # call never waits for earlier work on the stream.
+        src = idx64.contiguous()
+        if not src.is_pinned():
+            src = src.pin_memory()
+        idx = src.to(dev, non_blocking=True)
     status = ops.status_word(dev)
     stream = torch.cuda.current_stream(dev)
     check(lib().mskv_uva_gather(C.c_void_p(k_in.data_ptr()), C.c_void_p(v_in.data_ptr()),
