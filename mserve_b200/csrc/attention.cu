@@ -142,6 +142,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // and FMAs that made a CUDA-core version instruction bound.
 template <bool BF16, int D>
 __global__ void __launch_bounds__(kAtThreads) attn_mma_kernel(const AttnDev a) {
+  allow_dependents();  // the split merge may become resident as this grid drains
   constexpr int ROWB = D * 2;
   constexpr int ROWP = ROWB + 16;       // padded shared-memory row stride (bytes)
   constexpr int KS = D / 16;            // k-steps of Q·Kᵀ
@@ -343,6 +344,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_mma_kernel(const AttnDev a) {
 // one L2 round trip.
 template <typename T, int D>
 __global__ void __launch_bounds__(D) attn_merge_kernel(const AttnDev a) {
+  wait_for_previous_grid();  // the split partials come from attn_mma_kernel (programmatic launch)
   const int seg = blockIdx.x / a.nr, r = blockIdx.x - (blockIdx.x / a.nr) * a.nr;
   const int d = threadIdx.x;
   const int64_t wstride = (int64_t)a.nr * (D + 2);
@@ -509,13 +511,15 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
     int rc = after_launch("mskv_sparse_attention");
     if (rc) return rc;
     const unsigned mblocks = (unsigned)((int64_t)d->batch * d->kv_heads * a.nr);
+    cudaError_t e;
     if (d->head_dim == 128) {
-      if (bf) attn_merge_kernel<__nv_bfloat16, 128><<<mblocks, 128, 0, st>>>(a);
-      else attn_merge_kernel<__half, 128><<<mblocks, 128, 0, st>>>(a);
+      e = bf ? launch_dependent(attn_merge_kernel<__nv_bfloat16, 128>, dim3(mblocks), dim3(128), 0, st, a)
+             : launch_dependent(attn_merge_kernel<__half, 128>, dim3(mblocks), dim3(128), 0, st, a);
     } else {
-      if (bf) attn_merge_kernel<__nv_bfloat16, 64><<<mblocks, 64, 0, st>>>(a);
-      else attn_merge_kernel<__half, 64><<<mblocks, 64, 0, st>>>(a);
+      e = bf ? launch_dependent(attn_merge_kernel<__nv_bfloat16, 64>, dim3(mblocks), dim3(64), 0, st, a)
+             : launch_dependent(attn_merge_kernel<__half, 64>, dim3(mblocks), dim3(64), 0, st, a);
     }
+    if (e != cudaSuccess) return cuda_status(e, "mskv_sparse_attention merge launch");
     return after_launch("mskv_sparse_attention");
   }
   const int64_t rows = (int64_t)d->batch * d->q_heads * d->q_len;

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <utility>
 
 #include "mserve_kv.h"
 
@@ -22,6 +23,31 @@ int cuda_status(cudaError_t e, const char* what);
 extern std::atomic<uint64_t> g_launches;
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Programmatic dependent launch (sm_90 and later).  A kernel started with launch_dependent()
+// may become resident while the kernel before it in the stream is still running; it executes
+// wait_for_previous_grid() before touching any global memory, which returns once that kernel
+// has completed and its writes are visible.  The earlier kernel lets its dependents start
+// with allow_dependents() (without it they start when it exits).  Both are hardware
+// instructions; neither spins in software.
+__device__ __forceinline__ void wait_for_previous_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                    Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 inline int num_sms() {
   int dev = 0, n = 148;

@@ -98,6 +98,7 @@ __device__ __forceinline__ float reduce_scatter(float (&v)[N], int lane) {
 // memory (strided K, or paged K with page_size a multiple of GL).
 template <typename T, int D, int METHOD, bool PAGED>
 __global__ void __launch_bounds__(256) score_fast_kernel(const ScoreDev a) {
+  allow_dependents();  // the top-k kernel may become resident as this grid drains
   constexpr int EPV = Cvt<T>::EPV;
   constexpr int LPR = D / EPV;              // 16-byte chunks per row
   constexpr int GL = LPR < 16 ? LPR : 16;   // lanes per group (rows per group iteration)
@@ -365,6 +366,7 @@ __device__ __forceinline__ void gqa_query(const ScoreDev& a, int b, int h, int g
 // slice s+1 are issued before slice s is scored, so every lane always has 8 loads in flight.
 template <typename T, int D, int METHOD, bool PAGED>
 __global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) {
+  allow_dependents();  // the top-k kernel may become resident as this grid drains
   constexpr int GL = D / 8;
   static_assert(GL >= 8 && GL <= 32, "head_dim must be 64, 128 or 256");
   const int lane = threadIdx.x & 31;
@@ -433,6 +435,7 @@ static int launch_stream(ScoreDev& a, cudaStream_t st) {
 // Generic path: any head_dim, element-wise loads, one warp per row.
 template <typename T, int METHOD>
 __global__ void __launch_bounds__(256) score_generic_kernel(const ScoreDev a) {
+  allow_dependents();  // the top-k kernel may become resident as this grid drains
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;

@@ -120,6 +120,7 @@ __device__ __forceinline__ uint64_t block_exclusive_scan(uint64_t v, uint64_t* w
 }
 
 __global__ void __launch_bounds__(kTkThreads) topk_kernel(const TopkDev a) {
+  wait_for_previous_grid();  // the scores come from the kernel before (programmatic launch)
   __shared__ uint32_t hist[kTkWarps][256];
   __shared__ uint32_t tot[256];
   __shared__ uint32_t s_prefix, s_krem;
@@ -288,6 +289,7 @@ __device__ __forceinline__ void sm_digit_search(const uint32_t* hist, int nbins,
 }
 
 __global__ void __launch_bounds__(kSmThreads) topk_smem_kernel(const TopkDev a) {
+  wait_for_previous_grid();  // the scores come from the kernel before (programmatic launch)
   extern __shared__ __align__(16) uint32_t s_keys[];   // n keys, padded to a multiple of 4
   __shared__ __align__(16) uint32_t s_hist[kSmBins];
   __shared__ uint32_t s_wsuf[kSmWarps];
@@ -443,6 +445,7 @@ __device__ __forceinline__ void list_push(uint32_t* list, uint32_t* count, bool 
 
 __global__ void __cluster_dims__(kTcCtas, 1, 1) __launch_bounds__(kTcThreads)
     topk_cluster_kernel(const TopkDev a, int cap) {
+  wait_for_previous_grid();  // the scores come from the kernel before (programmatic launch)
   extern __shared__ uint32_t s_dyn[];
   __shared__ uint32_t s_hist[4][256];
   __shared__ uint32_t s_wsuf[8];
@@ -619,7 +622,9 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
       sm_attr_set = true;
     }
     const size_t smem = (size_t)((n_max + 3) / 4 * 4 + (n_max == 0 ? 4 : 0)) * sizeof(uint32_t);  // whole 4-key units
-    topk_smem_kernel<<<(unsigned)d->num_sel, kSmThreads, smem, as_stream(stream)>>>(a);
+    const cudaError_t e = launch_dependent(topk_smem_kernel, dim3((unsigned)d->num_sel), dim3(kSmThreads), smem,
+                                           as_stream(stream), a);
+    if (e != cudaSuccess) return cuda_status(e, "mskv_topk launch");
     return after_launch("mskv_topk");
   }
   const int64_t keys_per_cta = (n_max + kTcCtas - 1) / kTcCtas;
@@ -632,9 +637,13 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
     }
     const int cap = (int)(keys_per_cta > 0 ? keys_per_cta : 1);
     const size_t smem = 3 * (size_t)cap * sizeof(uint32_t);
-    topk_cluster_kernel<<<(unsigned)(d->num_sel * kTcCtas), kTcThreads, smem, as_stream(stream)>>>(a, cap);
+    const cudaError_t e = launch_dependent(topk_cluster_kernel, dim3((unsigned)(d->num_sel * kTcCtas)),
+                                           dim3(kTcThreads), smem, as_stream(stream), a, cap);
+    if (e != cudaSuccess) return cuda_status(e, "mskv_topk launch");
     return after_launch("mskv_topk");
   }
-  topk_kernel<<<d->num_sel, kTkThreads, 0, as_stream(stream)>>>(a);
+  const cudaError_t e = launch_dependent(topk_kernel, dim3((unsigned)d->num_sel), dim3(kTkThreads), 0,
+                                         as_stream(stream), a);
+  if (e != cudaSuccess) return cuda_status(e, "mskv_topk launch");
   return after_launch("mskv_topk");
 }
