@@ -355,6 +355,10 @@ def run_mserve(args, world, rank, local):
     numa_node = topology.numa_node(dev)
     barrier(world)
     peaks = pcie_peaks(dev)
+    # every rank measured at the same time: the sum is the host's aggregate link peak with all
+    # the job's GPUs pulling at once (the denominator of the whole-job rate)
+    peaks_all = {"h2d_sum": sum_over_ranks(peaks["h2d"], world), "d2h_sum": sum_over_ranks(peaks["d2h"], world),
+                 "note": "sum over ranks of the per-rank pinned memcpy peaks, measured concurrently"}
     gb_layer = gathered_bytes(eng)
     key_bytes_layer = eng.B * eng.Hkv * wl["seq_len"] * eng.D * 2
     stream = torch.cuda.current_stream(dev)
@@ -503,6 +507,8 @@ def run_mserve(args, world, rank, local):
                                                "the attention then reads its rows from L2"},
             "serial_ms_per_step": serial_ms_step, "chunks": args.chunks,
             "pcie_peak_gbs": peaks,
+            "pcie_peak_gbs_all_ranks": peaks_all,
+            "gather_frac_of_concurrent_h2d_peak_whole_step": value / peaks_all["h2d_sum"],
             "host_placement": {"numa_node": numa_node, "local_cpus": len(eng.host_cpus),
                                "note": "host store allocated on the GPU's local CPUs (0: placement left to the system)"}, "gather_frac_of_h2d_peak_whole_step": value / world / peaks["h2d"],
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),

@@ -16,7 +16,8 @@ tokens.  For each point it reports the gather GB/s (selected token rows = all he
 token, 2 KiB bf16 / 1 KiB fp8, host->HBM) and the write-back GB/s (the same number of rows,
 HBM->host ring positions), each against the pinned cudaMemcpyAsync peak of this GPU's host
 link in the same direction.  Under torchrun every rank runs the sweep on its own GPU and host
-link; rank 0 prints per-point aggregate GB/s (sum over ranks, time = max over ranks).
+link; rank 0 prints per-point aggregate GB/s (sum over ranks, time = max over ranks) against the
+aggregate memcpy peak (every rank's peak measured at the same time, summed).
 
 Prints one JSON object per line.
 """
@@ -146,7 +147,12 @@ def run_methods(args, device) -> dict:
 # ------------------------------------------------------------------------------- sweep mode
 def run_sweep(args, device, world: int, rank: int):
     T, H, D = args.sweep_tokens, 8, 128
-    peaks = memcpy_peaks(device)
+    # Every rank measures its memcpy peak at the same time; the sum over ranks is the host's
+    # aggregate link peak with all GPUs pulling at once, the denominator of the aggregate rate.
+    _barrier(world)
+    own = memcpy_peaks(device)
+    peaks = {"h2d": _sum(own["h2d"], world), "d2h": _sum(own["d2h"], world), "per_rank_h2d": own["h2d"],
+             "per_rank_d2h": own["d2h"], "ranks": world}
     gen = torch.Generator().manual_seed(4)
     lines = []
     for dtype in (torch.bfloat16, torch.float8_e4m3fn):
@@ -179,17 +185,32 @@ def run_sweep(args, device, world: int, rank: int):
                 nbytes = n_sel * row_bytes
                 ms_g = _max(ms_g, world)
                 ms_w = _max(ms_w, world)
-                agg = nbytes * world
+                agg = nbytes * world            # every rank moved nbytes; time = the slowest rank
                 line = {"mode": "sweep", "dtype": str(dtype).replace("torch.", ""), "tokens": T, "heads": H,
                         "head_dim": D, "density": density, "structure": "random" if run == 1 else f"runs{run}",
                         "rows": n_sel, "row_bytes": row_bytes, "n_gpus": world,
-                        "gather_gbs": agg / (ms_g * 1e-3) / 1e9, "gather_frac_h2d_peak": nbytes / (ms_g * 1e-3) / 1e9 / peaks["h2d"],
-                        "writeback_gbs": agg / (ms_w * 1e-3) / 1e9, "writeback_frac_d2h_peak": nbytes / (ms_w * 1e-3) / 1e9 / peaks["d2h"],
+                        "gather_gbs": agg / (ms_g * 1e-3) / 1e9, "gather_frac_h2d_peak": agg / (ms_g * 1e-3) / 1e9 / peaks["h2d"],
+                        "writeback_gbs": agg / (ms_w * 1e-3) / 1e9, "writeback_frac_d2h_peak": agg / (ms_w * 1e-3) / 1e9 / peaks["d2h"],
                         "gather_ms": ms_g, "writeback_ms": ms_w, "memcpy_peak_gbs": peaks, "bit_exact": True}
                 lines.append(line)
                 if rank == 0:
                     print(json.dumps(line), flush=True)
     return lines
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
 
 
 def _max(x: float, world: int) -> float:
