@@ -493,14 +493,10 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
     if (blocks > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "mskv_sparse_attention: grid too large");
     const bool bf = d->dtype == MSKV_DT_BF16;
     const int smem = (2 * kAtTile + 16) * (d->head_dim * 2 + 16);
-    static bool attr_set = false;  // benign race: every thread sets the same values
-    if (!attr_set) {
-      cudaFuncSetAttribute(attn_mma_kernel<true, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
-      cudaFuncSetAttribute(attn_mma_kernel<false, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
-      cudaFuncSetAttribute(attn_mma_kernel<true, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
-      cudaFuncSetAttribute(attn_mma_kernel<false, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
-      attr_set = true;
-    }
+    const void* kern = d->head_dim == 128 ? (bf ? (const void*)attn_mma_kernel<true, 128> : (const void*)attn_mma_kernel<false, 128>)
+                                          : (bf ? (const void*)attn_mma_kernel<true, 64> : (const void*)attn_mma_kernel<false, 64>);
+    int rc0 = ensure_smem_limit(kern, 80 * 1024, "mskv_sparse_attention");
+    if (rc0) return rc0;
     if (d->head_dim == 128) {
       if (bf) attn_mma_kernel<true, 128><<<(unsigned)blocks, kAtThreads, smem, st>>>(a);
       else attn_mma_kernel<false, 128><<<(unsigned)blocks, kAtThreads, smem, st>>>(a);

@@ -19,6 +19,9 @@ int fail(int code, const char* fmt, ...);
 int after_launch(const char* what);
 // Sets a message for a CUDA error and returns MSKV_ERR_CUDA (or MSKV_OK for cudaSuccess).
 int cuda_status(cudaError_t e, const char* what);
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device, once per
+// (kernel, device) in the process (the attribute is per device).  Thread-safe.
+int ensure_smem_limit(const void* kernel, int bytes, const char* what);
 
 extern std::atomic<uint64_t> g_launches;
 

@@ -2,7 +2,9 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "common.cuh"
 
@@ -24,6 +26,27 @@ int fail(int code, const char* fmt, ...) {
 int cuda_status(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return MSKV_OK;
   return fail(MSKV_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int ensure_smem_limit(const void* kernel, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, uint64_t> done;  // bit d: set on device d
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, what);
+  const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0;  // devices beyond 63: set every call
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (bit && (done[kernel] & bit)) return MSKV_OK;
+  }
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_status(e, what);
+  }
+  std::lock_guard<std::mutex> g(mu);
+  done[kernel] |= bit;
+  return MSKV_OK;
 }
 
 int after_launch(const char* what) {

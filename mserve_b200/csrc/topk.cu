@@ -615,12 +615,8 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
   // len_scalar bounds every len[b]; it sizes the per-CTA key buffer of the cluster path.
   const int64_t n_max = d->len_scalar > d->recent ? (int64_t)d->len_scalar - d->recent : 0;
   if (n_max <= kSmMaxKeys) {
-    static bool sm_attr_set = false;  // benign race: every thread sets the same value
-    if (!sm_attr_set) {
-      cudaFuncSetAttribute(topk_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kSmMaxKeys * (int)sizeof(uint32_t));
-      sm_attr_set = true;
-    }
+    int rc = ensure_smem_limit((const void*)topk_smem_kernel, kSmMaxKeys * (int)sizeof(uint32_t), "mskv_topk");
+    if (rc) return rc;
     const size_t smem = (size_t)((n_max + 3) / 4 * 4 + (n_max == 0 ? 4 : 0)) * sizeof(uint32_t);  // whole 4-key units
     const cudaError_t e = launch_dependent(topk_smem_kernel, dim3((unsigned)d->num_sel), dim3(kSmThreads), smem,
                                            as_stream(stream), a);
@@ -629,12 +625,8 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
   }
   const int64_t keys_per_cta = (n_max + kTcCtas - 1) / kTcCtas;
   if (keys_per_cta <= kTcMaxKeys && (int64_t)d->num_sel * kTcCtas <= 0x7fffffffLL) {
-    static bool attr_set = false;  // benign race: every thread sets the same value
-    if (!attr_set) {
-      cudaFuncSetAttribute(topk_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           3 * kTcMaxKeys * (int)sizeof(uint32_t));
-      attr_set = true;
-    }
+    int rc = ensure_smem_limit((const void*)topk_cluster_kernel, 3 * kTcMaxKeys * (int)sizeof(uint32_t), "mskv_topk");
+    if (rc) return rc;
     const int cap = (int)(keys_per_cta > 0 ? keys_per_cta : 1);
     const size_t smem = 3 * (size_t)cap * sizeof(uint32_t);
     const cudaError_t e = launch_dependent(topk_cluster_kernel, dim3((unsigned)(d->num_sel * kTcCtas)),
