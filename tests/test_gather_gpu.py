@@ -115,7 +115,7 @@ def test_gather_segments_ring_counts(built_lib, index_dtype, layout):
     assert (got_k[~mask] == 0).all()          # rows past the count are not written
 
 
-def test_gather_full_layer_config1(built_lib):
+def test_gather_full_7b_layer_4096_of_32768(built_lib):
     """One layer of the CPU-reference gather workload: K,V [32768 tokens, 4 KV heads, 128] bf16,
     4096 sorted unique indices -- bit-exact against index_select."""
     from mserve_b200 import cuda_uva
