@@ -43,7 +43,7 @@ class _Layer:
         self.len = 0            # logical tokens held
         self.version = 0
         self.pending: List[torch.cuda.Event] = []
-        self.start_dev = {}     # device index -> int32 [B] tensor of `start`
+        self.start_dev = {}     # device index -> (start, int32 [B] device tensor of it)
         self.lock = threading.Lock()
 
 
@@ -86,12 +86,15 @@ class CPUKVCache:
         layer.pending = []
 
     def _start_tensor(self, layer: _Layer, dev: torch.device) -> torch.Tensor:
+        """int32 [B] device tensor of the layer's ring start (cached with its host value, so
+        no call reads the device)."""
         idx = dev.index if dev.index is not None else torch.cuda.current_device()
-        t = layer.start_dev.get(idx)
-        if t is None or int(t[0].item()) != layer.start:
+        cached = layer.start_dev.get(idx)
+        if cached is None or cached[0] != layer.start:
             t = torch.full((layer.B,), layer.start, dtype=torch.int32, device=f"cuda:{idx}")
-            layer.start_dev[idx] = t
-        return t
+            layer.start_dev[idx] = (layer.start, t)
+            return t
+        return cached[1]
 
     # ------------------------------------------------------------------ append (write-back)
     def submit_append(self, layer_idx: int, key_new: torch.Tensor, value_new: torch.Tensor,
@@ -213,7 +216,12 @@ class CPUKVCache:
                     lo, hi = int(idx.min()), int(idx.max())
                     if lo < 0 or hi >= T:
                         raise RuntimeError(f"token index out of range [0, {T}): min {lo}, max {hi}")
-                idx = idx.to(dev)
+                # asynchronous H2D from page-locked memory (pinned staging for pageable input;
+                # torch keeps the pinned block until the copy has run): no host wait
+                idx = idx.contiguous()
+                if not idx.is_pinned():
+                    idx = idx.pin_memory()
+                idx = idx.to(dev, non_blocking=True)
             else:
                 idx = token_indices.to(dev)
                 if idx.dtype not in (torch.int32, torch.int64):
@@ -223,6 +231,7 @@ class CPUKVCache:
             k_out = torch.empty(layer.B, layer.H, S, layer.D, dtype=layer.dtype, device=dev)
             v_out = torch.empty_like(k_out)
             start_t = self._start_tensor(layer, dev)
+            start_t.record_stream(cur)      # the cached tensor may be replaced while this runs
             src = ops.strided_rows(layer.k, layer.v, len_scalar=T, ring_start=start_t, ring_cap=self.max_len,
                                    device=dev)
             ops.gather(src, idx, k_out, v_out, batch=layer.B)
@@ -269,6 +278,7 @@ class CPUKVCache:
             with layer.lock:
                 T = layer.len
                 start_t = self._start_tensor(layer, dev)
+                start_t.record_stream(stream)   # the cached tensor may be replaced while this runs
                 src = ops.strided_rows(layer.k, layer.v, len_scalar=T, ring_start=start_t, ring_cap=self.max_len,
                                        device=dev)
                 dst = ops.strided_rows(kb, vb, len_scalar=T, device=dev)
