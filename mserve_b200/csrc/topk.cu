@@ -69,6 +69,9 @@ __device__ __forceinline__ void load_keys(const TopkDev& a, const float* row0, i
       const int i = base + u * nthreads;
       v[u] = i < n ? row0[lo + i] : 0.f;
     }
+    // rows are added in order; unrolling lets the loads of consecutive rows be in flight
+    // together (the adds stay in row order)
+#pragma unroll(NL >= 16 ? 2 : 4)
     for (int r = 1; r < a.rows_per_sel; ++r) {
       const float* rr = row0 + (int64_t)(r / a.row_block) * a.block_stride + (int64_t)(r % a.row_block) * a.ss;
 #pragma unroll
@@ -614,7 +617,11 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
   a.block_stride = d->block_stride;
   // len_scalar bounds every len[b]; it sizes the per-CTA key buffer of the cluster path.
   const int64_t n_max = d->len_scalar > d->recent ? (int64_t)d->len_scalar - d->recent : 0;
-  if (n_max <= kSmMaxKeys) {
+  // One CTA per selection reads rows_per_sel x n scores through one SM.  When each selection
+  // sums several rows over many tokens and there are few selections, the 8-CTA cluster spreads
+  // that load over 8 SMs per selection instead.
+  const bool wide_load = d->rows_per_sel >= 4 && n_max >= 8192 && (int64_t)d->num_sel * kTcCtas <= 2 * num_sms();
+  if (n_max <= kSmMaxKeys && !wide_load) {
     int rc = ensure_smem_limit((const void*)topk_smem_kernel, kSmMaxKeys * (int)sizeof(uint32_t), "mskv_topk");
     if (rc) return rc;
     const size_t smem = (size_t)((n_max + 3) / 4 * 4 + (n_max == 0 ? 4 : 0)) * sizeof(uint32_t);  // whole 4-key units

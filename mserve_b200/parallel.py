@@ -50,6 +50,9 @@ def exchange_head_scores(local: torch.Tensor, gathered: torch.Tensor, group=None
         raise ValueError("score buffers must be contiguous")
     if gathered.numel() != world * local.numel():
         raise ValueError(f"gathered holds {gathered.numel()} elements, expected {world} x {local.numel()}")
+    if world == 1:                       # one rank holds every head: a device copy
+        gathered.view_as(local).copy_(local)
+        return gathered
     dist.all_gather_into_tensor(gathered.view(world * local.shape[0], *local.shape[1:]), local, group=group)
     return gathered
 

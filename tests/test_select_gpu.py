@@ -202,3 +202,23 @@ def test_topk_len_above_len_scalar_is_clamped(built_lib):
     np.testing.assert_array_equal(cnt, rcnt)
     for j in range(2):
         np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
+
+
+def test_topk_summed_rows_cluster_path(built_lib):
+    """Few selections that sum several head rows over many tokens (the reference's head mean)
+    take the 8-CTA cluster path: exact against the oracle with ties, NaN and ragged lengths."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(77)
+    B, Hk, T = 3, 4, 20000
+    rows = (torch.randn(B * Hk, T, generator=g) * 8).round() * 0.125
+    rows[2, 99] = float("nan")
+    lens = torch.tensor([T, 15000, 9000], dtype=torch.int32)
+    topk_b = torch.tensor([3000, 1, 4321], dtype=torch.int32)
+    got, cnt = ops.topk(rows.cuda(), top_k=topk_b.cuda(), recent=64, len_=lens.cuda(), rows_per_sel=Hk,
+                        sel_per_batch=1, scale=1.0 / 28)
+    ref, rcnt = ko.select_topk_window(rows.numpy(), top_k=topk_b.numpy(), recent=64, lens=lens.numpy(),
+                                      rows_per_sel=Hk, sel_per_batch=1, scale=np.float32(1.0 / 28))
+    got, cnt = got.cpu().numpy(), cnt.cpu().numpy()
+    np.testing.assert_array_equal(cnt, rcnt)
+    for j in range(B):
+        np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
