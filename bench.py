@@ -35,10 +35,19 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "selected-KV gather GB/s host→HBM vs PCIe peak; decode step ms at 1/2/4/8 B200"
-WORKLOAD = dict(layers=28, batch=8, q_heads=28, kv_heads=4, head_dim=128, seq_len=16384, top_k=2048, recent=128,
-                image_frac=0.75)
-WORKLOAD_NAME = ("qwen2.5-vl-7b decode selection: 28 layers, 28q/4kv heads, head_dim 128, bf16, 8 seqs x 16384 "
-                 "tokens per GPU, top-2048 + last-128 per (seq, kv head), KV in pinned host")
+# The decode-selection workloads.  image_frac: the first fraction of every sequence's KV is
+# ~N(0,1) ("image" tokens), the rest ~N(0,0.5) ("text").
+WORKLOADS = {
+    "qwen7b": (dict(layers=28, batch=8, q_heads=28, kv_heads=4, head_dim=128, seq_len=16384, top_k=2048,
+                    recent=128, image_frac=0.75),
+               "qwen2.5-vl-7b decode selection: 28 layers, 28q/4kv heads, head_dim 128, bf16, 8 seqs x 16384 "
+               "tokens per GPU, top-2048 + last-128 per (seq, kv head), KV in pinned host"),
+    "qwen32b": (dict(layers=64, batch=16, q_heads=40, kv_heads=8, head_dim=128, seq_len=32768, top_k=4096,
+                     recent=256, image_frac=1.0),
+                "qwen2.5-vl-32b decode selection: 64 layers, 40q/8kv heads, head_dim 128, bf16, 16 seqs x 32768 "
+                "tokens per GPU, KV ~N(0,1), top-4096 + last-256 per (seq, kv head), KV in pinned host"),
+}
+WORKLOAD, WORKLOAD_NAME = WORKLOADS["qwen7b"]
 
 
 def parse():
@@ -51,6 +60,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--chunks", type=int, default=4, help="sequence chunks pipelined per layer")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen7b",
+                    help="qwen7b (the headline workload) or qwen32b (64 layers need ~140 GB of pinned host "
+                         "memory per GPU: use --layers on smaller hosts)")
     return ap.parse_args()
 
 
@@ -300,7 +312,7 @@ def run_reference(args, world, rank):
     """The reference's CPU path (C restatement) on the host cores; rank 0 only."""
     if rank != 0:
         return
-    wl = dict(WORKLOAD)
+    wl = dict(WORKLOADS[args.workload][0])
     if args.layers:
         wl["layers"] = args.layers
     sample_layers = min(4, wl["layers"])
@@ -334,7 +346,8 @@ def run_reference(args, world, rank):
         "metric": METRIC, "value": value, "unit": "GB/s", "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD_NAME, "global_batch": B, "seq_len": T, "parallelism": "host cores, rank 0"},
+        "config": {"workload": WORKLOADS[args.workload][1], "global_batch": B, "seq_len": T,
+                   "parallelism": "host cores, rank 0"},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": nth, "kind": "port", "sample": sample,
                          "cpu": cpu_model()},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -345,7 +358,7 @@ def run_reference(args, world, rank):
 def run_mserve(args, world, rank, local):
     from mserve_b200 import _lib, ops
     dev = torch.device("cuda", local)
-    wl = dict(WORKLOAD)
+    wl = dict(WORKLOADS[args.workload][0])
     if args.layers:
         wl["layers"] = args.layers
     L = wl["layers"]
@@ -496,7 +509,8 @@ def run_mserve(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD_NAME if L == 28 else WORKLOAD_NAME + f" (layers overridden: {L})",
+            "config": {"workload": (WORKLOADS[args.workload][1] if L == WORKLOADS[args.workload][0]["layers"]
+                                    else WORKLOADS[args.workload][1] + f" (layers overridden: {L})"),
                        "global_batch": wl["batch"] * world, "seq_len": wl["seq_len"],
                        "parallelism": f"{world} rank(s), each its own 8 sequences over its own host link, "
                                       "no collective on the data path",
