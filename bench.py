@@ -46,7 +46,25 @@ WORKLOADS = {
                      recent=256, image_frac=1.0),
                 "qwen2.5-vl-32b decode selection: 64 layers, 40q/8kv heads, head_dim 128, bf16, 16 seqs x 32768 "
                 "tokens per GPU, KV ~N(0,1), top-4096 + last-256 per (seq, kv head), KV in pinned host"),
+    # multi-turn: context lengths uniform in [4096, 65536] (seed 3); one timed turn appends 2880
+    # image + 64 text tokens per sequence (16-token HBM key pages + host write-through), then
+    # decode selects the top ceil(10% of L_b) tokens per (sequence, KV head)
+    "llava34b": (dict(layers=60, batch=32, q_heads=56, kv_heads=8, head_dim=128, seq_len=65536, top_k=0,
+                      top_k_ratio=0.1, recent=0, image_frac=1.0, lens_uniform=(4096, 65536), lens_seed=3,
+                      turn_image=2880, turn_text=64),
+                 "llava-v1.6-34b multi-turn decode selection: 60 layers, 56q/8kv heads, head_dim 128, bf16, 32 seqs "
+                 "with contexts uniform in [4096, 65536], a 2880 image + 64 text token append turn, then top-10% "
+                 "per (seq, kv head), KV in pinned host"),
 }
+
+
+def workload_lens(wl):
+    """Context length of every sequence of the workload."""
+    if "lens_uniform" in wl:
+        lo, hi = wl["lens_uniform"]
+        rng = np.random.default_rng(wl["lens_seed"])
+        return [int(x) for x in rng.integers(lo, hi, size=wl["batch"], endpoint=True)]
+    return [wl["seq_len"]] * wl["batch"]
 WORKLOAD, WORKLOAD_NAME = WORKLOADS["qwen7b"]
 
 
@@ -203,10 +221,12 @@ NCU_SYSMEM_BYTES = {"gather": (1048576 + 65536) * 32}
 def build_engine(wl, device, seed):
     from mserve_b200.engine import OffloadKV
     L, B, Hq, Hkv, D, T = (wl[k] for k in ("layers", "batch", "q_heads", "kv_heads", "head_dim", "seq_len"))
-    eng = OffloadKV(L, B, Hq, Hkv, D, T + 256, top_k=wl["top_k"], recent=wl["recent"], device=device)
+    turn = wl.get("turn_image", 0) + wl.get("turn_text", 0)
+    eng = OffloadKV(L, B, Hq, Hkv, D, T + 256 + turn, top_k=wl["top_k"], recent=wl["recent"],
+                    top_k_ratio=wl.get("top_k_ratio"), device=device)
     g = torch.Generator(device=device).manual_seed(seed)
     n_img = int(T * wl["image_frac"])
-    eng.reserve([T] * B)
+    eng.reserve(workload_lens(wl))
     for layer in range(L):
         k = torch.randn(B, Hkv, T, D, generator=g, device=device, dtype=torch.float32)
         v = torch.randn(B, Hkv, T, D, generator=g, device=device, dtype=torch.float32)
@@ -221,8 +241,39 @@ def build_engine(wl, device, seed):
 
 
 def gathered_bytes(eng):
-    """Selected K+V bytes per decode layer (counts are fixed: top_k + recent per segment)."""
-    return 2 * eng.B * eng.Hkv * eng.S * eng.D * torch.empty((), dtype=eng.dtype).element_size()
+    """Selected K+V bytes per decode layer: per segment min(k_b, L_b - R) + min(R, L_b) rows."""
+    lens = eng.len_h.astype(np.int64)
+    n = np.maximum(lens - eng.recent, 0)
+    k = eng.topk_h if eng.top_k_ratio is not None else np.full(eng.B, eng.top_k, dtype=np.int64)
+    rows = int((np.minimum(k, n) + (lens - n)).sum()) * eng.Hkv
+    return 2 * rows * eng.D * torch.empty((), dtype=eng.dtype).element_size()
+
+
+def append_turn(eng, wl, device, seed):
+    """Appends one turn (image then text tokens) to every sequence of every layer, timed with CUDA
+    events: returns (ms, bytes written to the host store, bytes written to HBM key pages)."""
+    turn_img, turn_txt = wl.get("turn_image", 0), wl.get("turn_text", 0)
+    n = turn_img + turn_txt
+    B, Hkv, D = eng.B, eng.Hkv, eng.D
+    g = torch.Generator(device=device).manual_seed(seed)
+    rows = []
+    for _ in range(eng.L):                 # the new rows exist before the timed region
+        k = torch.randn(B, Hkv, n, D, generator=g, device=device)
+        v = torch.randn(B, Hkv, n, D, generator=g, device=device)
+        k[:, :, turn_img:] *= 0.5
+        v[:, :, turn_img:] *= 0.5
+        rows.append((k.to(torch.bfloat16), v.to(torch.bfloat16)))
+    torch.cuda.synchronize(device)
+    eng.reserve([n] * B)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for layer, (k, v) in enumerate(rows):
+        eng.append_layer(layer, k, v)
+    e1.record()
+    e1.synchronize()
+    eng.commit()
+    es = torch.empty((), dtype=eng.dtype).element_size()
+    return e0.elapsed_time(e1), 2 * eng.L * B * Hkv * n * D * es, eng.L * B * Hkv * n * D * es
 
 
 # ------------------------------------------------------------------------------------- CPU path
@@ -363,6 +414,13 @@ def run_mserve(args, world, rank, local):
         wl["layers"] = args.layers
     L = wl["layers"]
     eng, q = build_engine(wl, dev, seed=1000 + rank)
+    turn = None
+    if wl.get("turn_image", 0) + wl.get("turn_text", 0):
+        ms, host_bytes, page_bytes = append_turn(eng, wl, dev, seed=2000 + rank)
+        turn = {"ms": ms, "host_write_bytes": host_bytes, "hbm_page_bytes": page_bytes,
+                "host_write_gbs": host_bytes / (ms * 1e-3) / 1e9,
+                "note": "one append turn over all layers: K rows into HBM key pages and K+V rows written "
+                        "through to the pinned host store (mskv_copy_rows), CUDA events"}
     bufs = eng.buffers()
     from mserve_b200 import topology
     numa_node = topology.numa_node(dev)
@@ -373,7 +431,7 @@ def run_mserve(args, world, rank, local):
     peaks_all = {"h2d_sum": sum_over_ranks(peaks["h2d"], world), "d2h_sum": sum_over_ranks(peaks["d2h"], world),
                  "note": "sum over ranks of the per-rank pinned memcpy peaks, measured concurrently"}
     gb_layer = gathered_bytes(eng)
-    key_bytes_layer = eng.B * eng.Hkv * wl["seq_len"] * eng.D * 2
+    key_bytes_layer = int(eng.len_h.sum()) * eng.Hkv * eng.D * 2
     stream = torch.cuda.current_stream(dev)
 
     # The product path: the whole decode step (all layers, chunk-pipelined over three streams)
@@ -469,7 +527,8 @@ def run_mserve(args, world, rank, local):
 
     # CPU baseline: the C restatement on this host's cores, rank 0 at N=1 only
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    fixed_shape = "lens_uniform" not in wl and "top_k_ratio" not in wl   # what the C port restates
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and fixed_shape:
         nth = cpu_threads()
         hk, hv = host_views(eng)
         qn = q.cpu().view(torch.int16).numpy().view(np.uint16)
@@ -520,6 +579,7 @@ def run_mserve(args, world, rank, local):
                                        "note": "each phase of all layers replayed alone as a CUDA graph after the timed region; "
                                                "the attention then reads its rows from L2"},
             "serial_ms_per_step": serial_ms_step, "chunks": args.chunks,
+            "append_turn": turn,
             "pcie_peak_gbs": peaks,
             "pcie_peak_gbs_all_ranks": peaks_all,
             "gather_frac_of_concurrent_h2d_peak_whole_step": value / peaks_all["h2d_sum"],
