@@ -251,31 +251,110 @@ struct SliceRef {
   bool ok;    // this lane group has rows and their page is mapped
 };
 
-// A warp's position in its run of slices: segment (b, h) and slice index within it.  The
-// segment fields are updated incrementally, so no slice needs an integer division.
+// A warp's position in its run of slices: segment (b, h), slice index within it, and the
+// sequence's length and live slice count.  Only slices that hold tokens ("live": sequence b
+// has ceil(min(len_b, max_tokens) / RPW) per KV head) are numbered, so every warp gets an equal
+// share of real work however ragged the lengths are; the fields are updated incrementally.
 struct SliceCursor {
-  int64_t seg, sis, len;
+  int64_t seg;
+  int len, live, sis;   // tokens per sequence fit in 31 bits (max_tokens is checked on the host)
   int b, h;
 };
 
-__device__ __forceinline__ void cursor_init(const ScoreDev& a, SliceCursor& c, int64_t s) {
-  c.seg = s / a.slices_per_seg;
-  c.sis = s - c.seg * a.slices_per_seg;
-  c.b = (int)(c.seg / a.kv_heads);
-  c.h = (int)(c.seg - (int64_t)c.b * a.kv_heads);
-  c.len = rows_len(a.k, c.b);
+template <int RPW>
+__device__ __forceinline__ int live_slices(const ScoreDev& a, int b, int* len_out = nullptr) {
+  int64_t len = rows_len(a.k, b);
+  len = len < 0 ? 0 : (len > a.max_tokens ? a.max_tokens : len);   // max_tokens bounds the scores rows
+  if (len_out) *len_out = (int)len;
+  return (int)((len + RPW - 1) / RPW);
 }
 
-__device__ __forceinline__ void cursor_next(const ScoreDev& a, SliceCursor& c) {
-  if (++c.sis == a.slices_per_seg) {
-    c.sis = 0;
-    ++c.seg;
-    if (++c.h == a.kv_heads) {
-      c.h = 0;
-      ++c.b;
-      if (c.b < a.batch) c.len = rows_len(a.k, c.b);
+// Warp-collective: this warp's share [begin, begin + count) of the live slices of the grid,
+// and the cursor at its first slice.  Returns false for a warp without work.
+template <int RPW>
+__device__ __forceinline__ bool cursor_init(const ScoreDev& a, int64_t warp, int64_t nwarps, SliceCursor& c,
+                                            int64_t& count) {
+  const int lane = threadIdx.x & 31;
+  if (a.batch <= 32) {                         // one pass: lane b holds sequence b
+    int len_b = 0;
+    const int live_b = lane < a.batch ? live_slices<RPW>(a, lane, &len_b) : 0;
+    const int64_t v = (int64_t)live_b * a.kv_heads;
+    int64_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
     }
+    const int64_t total = __shfl_sync(0xffffffffu, inc, 31);
+    const int64_t per = (total + nwarps - 1) / nwarps;
+    const int64_t begin = warp * per;
+    const int64_t end = min(begin + per, total);
+    if (begin >= end) return false;
+    count = end - begin;
+    const int l = __ffs(__ballot_sync(0xffffffffu, inc > begin)) - 1;
+    const int64_t off = begin - __shfl_sync(0xffffffffu, inc - v, l);
+    c.b = l;
+    c.live = __shfl_sync(0xffffffffu, live_b, l);
+    c.len = __shfl_sync(0xffffffffu, len_b, l);
+    c.h = (int)(off / c.live);
+    c.sis = (int)(off - (int64_t)c.h * c.live);
+    c.seg = (int64_t)c.b * a.kv_heads + c.h;
+    return true;
   }
+  int64_t total = 0;
+  for (int b0 = 0; b0 < a.batch; b0 += 32) {
+    const int b = b0 + lane;
+    int64_t v = b < a.batch ? (int64_t)live_slices<RPW>(a, b) * a.kv_heads : 0;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    total += v;
+  }
+  const int64_t per = (total + nwarps - 1) / nwarps;
+  const int64_t begin = warp * per;
+  const int64_t end = min(begin + per, total);
+  if (begin >= end) return false;
+  count = end - begin;
+  int64_t base = 0;
+  for (int b0 = 0; b0 < a.batch; b0 += 32) {
+    const int b = b0 + lane;
+    const int64_t v = b < a.batch ? (int64_t)live_slices<RPW>(a, b) * a.kv_heads : 0;
+    int64_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    const int64_t chunk_total = __shfl_sync(0xffffffffu, inc, 31);
+    if (begin < base + chunk_total) {            // warp-uniform
+      const int l = __ffs(__ballot_sync(0xffffffffu, base + inc > begin)) - 1;
+      const int64_t before = base + __shfl_sync(0xffffffffu, inc - v, l);
+      c.b = b0 + l;
+      c.live = live_slices<RPW>(a, c.b, &c.len);
+      const int64_t off = begin - before;
+      c.h = (int)(off / c.live);
+      c.sis = (int)(off - (int64_t)c.h * c.live);
+      c.seg = (int64_t)c.b * a.kv_heads + c.h;
+      return true;
+    }
+    base += chunk_total;
+  }
+  return false;
+}
+
+template <int RPW>
+__device__ __forceinline__ void cursor_next(const ScoreDev& a, SliceCursor& c) {
+  if (++c.sis < c.live) return;
+  c.sis = 0;
+  if (++c.h < a.kv_heads) {
+    ++c.seg;
+    return;
+  }
+  c.h = 0;
+  do {                                           // the next sequence that holds tokens
+    ++c.b;
+    c.live = c.b < a.batch ? live_slices<RPW>(a, c.b, &c.len) : 1;
+  } while (c.live == 0);
+  c.seg = (int64_t)c.b * a.kv_heads;
 }
 
 template <int D, bool PAGED>
@@ -286,7 +365,7 @@ __device__ __forceinline__ SliceRef locate_slice(const ScoreDev& a, const SliceC
   r.b = c.b;
   r.h = c.h;
   r.len = c.len;
-  const int64_t t_slice = c.sis * RPW;
+  const int64_t t_slice = (int64_t)c.sis * RPW;
   r.live = t_slice < r.len;
   r.t0 = t_slice + grp * 8;
   r.ok = r.t0 < r.len;
@@ -371,13 +450,12 @@ __global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) 
   static_assert(GL >= 8 && GL <= 32, "head_dim must be 64, 128 or 256");
   const int lane = threadIdx.x & 31;
   const int gl = lane % GL, grp = lane / GL;
+  constexpr int RPW = 8 * (32 / GL);
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t s_begin = warp * a.slices_per_warp;
-  const int64_t s_end = min(s_begin + a.slices_per_warp, a.total_slices);
-  if (s_begin >= s_end) return;
-
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   SliceCursor cur_pos;
-  cursor_init(a, cur_pos, s_begin);
+  int64_t count = 0;
+  if (!cursor_init<RPW>(a, warp, nwarps, cur_pos, count)) return;
   float2 qs[4];
   int64_t q_seg = -1;
   auto score = [&](const SliceRef& r, const uint4 (&raw)[8]) {
@@ -394,19 +472,19 @@ __global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) 
   uint4 bufA[8], bufB[8];
   SliceRef cur = locate_slice<D, PAGED>(a, cur_pos, grp);
   issue_rows(a, cur, gl, bufA);
-  for (int64_t s = s_begin; s < s_end; s += 2) {
+  for (int64_t s = 0; s < count; s += 2) {
     SliceRef nxt;
-    const bool has1 = s + 1 < s_end;
+    const bool has1 = s + 1 < count;
     if (has1) {
-      cursor_next(a, cur_pos);
+      cursor_next<RPW>(a, cur_pos);
       nxt = locate_slice<D, PAGED>(a, cur_pos, grp);
       issue_rows(a, nxt, gl, bufB);
     }
     score(cur, bufA);
     if (!has1) break;
-    const bool has2 = s + 2 < s_end;
+    const bool has2 = s + 2 < count;
     if (has2) {
-      cursor_next(a, cur_pos);
+      cursor_next<RPW>(a, cur_pos);
       cur = locate_slice<D, PAGED>(a, cur_pos, grp);
       issue_rows(a, cur, gl, bufA);
     }
@@ -538,6 +616,7 @@ extern "C" int mskv_score(const mskv_score_desc* d, void* stream) {
   int rc = check_rows(d->k, "mskv_score k", false);
   if (rc) return rc;
   if (d->scores_stride < d->max_tokens) return fail(MSKV_ERR_ARG, "mskv_score: scores_stride < max_tokens");
+  if (d->max_tokens > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "mskv_score: max_tokens exceeds 31 bits");
   if (d->batch == 0 || d->max_tokens == 0) return MSKV_OK;
   int es;
   switch (d->dtype) {

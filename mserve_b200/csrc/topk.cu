@@ -225,8 +225,8 @@ __global__ void __launch_bounds__(kTkThreads) topk_kernel(const TopkDev a) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Shared-memory path (up to kSmMaxKeys candidates): one 1024-thread CTA per selection keeps
-// every candidate key in shared memory, so no step needs more than __syncthreads.
+// Shared-memory path (up to kSmMaxKeys candidates per CTA): one 1024-thread CTA per selection
+// (two, as a cluster, up to 2 x kSmMaxKeys) keeps every candidate key in shared memory.
 //
 // Digits of 12, 12 and 8 bits: the first pass histograms every key into 4096 bins (plain
 // shared atomics; a 12-bit digit of an fp32 key spans an eighth of a binade, so real scores
@@ -246,16 +246,13 @@ __device__ __forceinline__ uint32_t lanemask_lt_sm() {
 
 // Finds the bin holding the krem-th largest key of the histogram (bins ordered by value);
 // sets *prefix |= bin << shift and *krem to the rank within that bin.  Every thread calls it.
-__device__ __forceinline__ void sm_digit_search(const uint32_t* hist, int nbins, int shift, uint32_t* s_wsuf,
+// Finds the bin holding the krem-th largest key (bins ordered by value) from the 4 bin counts
+// c[0..3] each thread owns (bins 4t .. 4t+3); sets prefix |= bin << shift and krem to the rank
+// within that bin.  Every thread of the CTA calls it.
+__device__ __forceinline__ void sm_digit_search(const uint32_t (&c)[4], int shift, uint32_t* s_wsuf,
                                                 uint32_t* s_prefix, uint32_t* s_krem, uint32_t& prefix,
                                                 uint32_t& krem) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // thread t owns bins [4t, 4t+4)
-  uint32_t c[4] = {0, 0, 0, 0};
-  if (4 * tid < nbins) {
-    const uint4 v = reinterpret_cast<const uint4*>(hist)[tid];
-    c[0] = v.x; c[1] = v.y; c[2] = v.z; c[3] = v.w;
-  }
   const uint32_t own = c[0] + c[1] + c[2] + c[3];
   uint32_t suf = own;  // inclusive suffix over the lanes of the warp
 #pragma unroll
@@ -291,15 +288,49 @@ __device__ __forceinline__ void sm_digit_search(const uint32_t* hist, int nbins,
   krem = *s_krem;
 }
 
+// The thread's 4 bins of a histogram, summed over the NCTA CTAs of the cluster (distributed
+// shared memory); bins at or beyond nbins count 0.
+template <int NCTA>
+__device__ __forceinline__ void cluster_bins(uint32_t (&c)[4], uint32_t* hist, int nbins) {
+  c[0] = c[1] = c[2] = c[3] = 0;
+  if (4 * (int)threadIdx.x >= nbins) return;
+  const uint4 v = reinterpret_cast<const uint4*>(hist)[threadIdx.x];
+  c[0] = v.x; c[1] = v.y; c[2] = v.z; c[3] = v.w;
+  if constexpr (NCTA > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned me = cluster.block_rank();
+#pragma unroll
+    for (int r = 0; r < NCTA; ++r) {
+      if ((unsigned)r == me) continue;
+      const uint4 w = reinterpret_cast<const uint4*>(cluster.map_shared_rank(hist, r))[threadIdx.x];
+      c[0] += w.x; c[1] += w.y; c[2] += w.z; c[3] += w.w;
+    }
+  }
+}
+
+template <int NCTA>
+__device__ __forceinline__ void cta_group_sync() {
+  if constexpr (NCTA > 1) cg::this_cluster().sync();
+  else __syncthreads();
+}
+
+// One selection per NCTA CTAs (NCTA = 1, or a 2-CTA cluster for up to 2 x kSmMaxKeys
+// candidates): CTA r holds the keys [r*chunk, (r+1)*chunk) in shared memory.  Every radix pass
+// has its own histogram buffer, so no buffer is cleared while the peer CTA may still read it.
+template <int NCTA>
 __global__ void __launch_bounds__(kSmThreads) topk_smem_kernel(const TopkDev a) {
   wait_for_previous_grid();  // the scores come from the kernel before (programmatic launch)
-  extern __shared__ __align__(16) uint32_t s_keys[];   // n keys, padded to a multiple of 4
-  __shared__ __align__(16) uint32_t s_hist[kSmBins];
+  extern __shared__ __align__(16) uint32_t s_keys[];   // this CTA's keys, padded to a multiple of 4
+  __shared__ __align__(16) uint32_t s_hist0[kSmBins];
+  __shared__ __align__(16) uint32_t s_hist1[kSmBins];
+  __shared__ __align__(16) uint32_t s_hist2[256];
   __shared__ uint32_t s_wsuf[kSmWarps];
   __shared__ uint64_t s_wcnt[kSmWarps];
+  __shared__ uint64_t s_cnt;
   __shared__ uint32_t s_prefix, s_krem;
 
-  const int64_t j = blockIdx.x;
+  const int rank = NCTA > 1 ? (int)cg::this_cluster().block_rank() : 0;
+  const int64_t j = blockIdx.x / NCTA;
   const int b = (int)(j / a.sel_per_batch);
   // len_scalar bounds every len[b] (it sized the key buffer): a larger len[b] is clamped
   const int64_t L = a.len ? min((int64_t)a.len[b], (int64_t)a.len_scalar) : (int64_t)a.len_scalar;
@@ -310,55 +341,58 @@ __global__ void __launch_bounds__(kSmThreads) topk_smem_kernel(const TopkDev a) 
   const int64_t w = L - n;
   const float* row0 = a.scores + j * a.sel_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chunk = (n + NCTA - 1) / NCTA;
+  const int lo = min(rank * chunk, n), m = min(lo + chunk, n) - lo;   // this CTA's keys [lo, lo + m)
   const uint4* keys4 = reinterpret_cast<const uint4*>(s_keys);
-  const int n4 = (n + 3) >> 2;  // 4-key units; the last may be partial (its tail is masked)
+  const int m4 = (m + 3) >> 2;  // 4-key units; the last may be partial (its tail is masked)
 
   if (K > 0 && K < n) {
-    for (int i = tid; i < kSmBins; i += kSmThreads) s_hist[i] = 0;
+    for (int i = tid; i < kSmBins; i += kSmThreads) { s_hist0[i] = 0; s_hist1[i] = 0; }
+    if (tid < 256) s_hist2[tid] = 0;
     __syncthreads();
     // keys into shared memory; digit 0 (bits 31..20) histogrammed on the way
-    load_keys<16>(a, row0, 0, n, s_keys, tid, kSmThreads, s_hist, 20);
-    __syncthreads();
-    uint32_t prefix = 0, krem = (uint32_t)K;
-    sm_digit_search(s_hist, kSmBins, 20, s_wsuf, &s_prefix, &s_krem, prefix, krem);
+    load_keys<16>(a, row0, lo, m, s_keys, tid, kSmThreads, s_hist0, 20);
+    cta_group_sync<NCTA>();
+    uint32_t prefix = 0, krem = (uint32_t)K, c[4];
+    cluster_bins<NCTA>(c, s_hist0, kSmBins);
+    sm_digit_search(c, 20, s_wsuf, &s_prefix, &s_krem, prefix, krem);
     // digit 1: bits 19..8 of the keys whose top 12 bits match
-    for (int i = tid; i < kSmBins; i += kSmThreads) s_hist[i] = 0;
-    __syncthreads();
-    for (int u = tid; u < n4; u += kSmThreads) {
+    for (int u = tid; u < m4; u += kSmThreads) {
       const uint4 kv = keys4[u];
       const uint32_t k4[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        if (4 * u + e < n && (k4[e] >> 20) == (prefix >> 20)) atomicAdd(&s_hist[(k4[e] >> 8) & 0xfffu], 1u);
+        if (4 * u + e < m && (k4[e] >> 20) == (prefix >> 20)) atomicAdd(&s_hist1[(k4[e] >> 8) & 0xfffu], 1u);
     }
-    __syncthreads();
-    sm_digit_search(s_hist, kSmBins, 8, s_wsuf, &s_prefix, &s_krem, prefix, krem);
+    cta_group_sync<NCTA>();
+    cluster_bins<NCTA>(c, s_hist1, kSmBins);
+    sm_digit_search(c, 8, s_wsuf, &s_prefix, &s_krem, prefix, krem);
     // digit 2: bits 7..0 of the keys whose top 24 bits match
-    for (int i = tid; i < 256; i += kSmThreads) s_hist[i] = 0;
-    __syncthreads();
-    for (int u = tid; u < n4; u += kSmThreads) {
+    for (int u = tid; u < m4; u += kSmThreads) {
       const uint4 kv = keys4[u];
       const uint32_t k4[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        if (4 * u + e < n && (k4[e] >> 8) == (prefix >> 8)) atomicAdd(&s_hist[k4[e] & 0xffu], 1u);
+        if (4 * u + e < m && (k4[e] >> 8) == (prefix >> 8)) atomicAdd(&s_hist2[k4[e] & 0xffu], 1u);
     }
-    __syncthreads();
-    sm_digit_search(s_hist, 256, 0, s_wsuf, &s_prefix, &s_krem, prefix, krem);
+    cta_group_sync<NCTA>();
+    cluster_bins<NCTA>(c, s_hist2, 256);
+    sm_digit_search(c, 0, s_wsuf, &s_prefix, &s_krem, prefix, krem);
 
-    // Ordered compaction through bitmaps.  Word q covers keys [32q, 32q+32), bit i = key 32q+i:
-    // G_q marks keys above the threshold key, E_q keys equal to it (one ballot pair per word).
-    // A block scan of (#G, #E) per word gives every word its output position and how many of
-    // the equal keys before it were kept; its thread then writes only its selected keys.
-    const int nw = (n + 31) >> 5;                 // <= kSmMaxKeys / 32 = 1536 words
-    uint32_t* s_g = s_hist;                       // the histogram is free now
-    uint32_t* s_e = s_hist + kSmMaxKeys / 32;
-    __syncthreads();                              // the last digit search read s_hist
+    // Ordered compaction through bitmaps.  Word q covers this CTA's keys [32q, 32q+32), bit i =
+    // key lo + 32q + i: G_q marks keys above the threshold key, E_q keys equal to it (one
+    // ballot pair per word).  A block scan of (#G, #E) per word, offset by the counts of the
+    // lower-ranked CTA, gives every word its output position and how many equal keys before it
+    // were kept; its thread then writes only its selected keys.  s_hist0 holds the words: every
+    // CTA finished reading the peers' digit-0 histograms before the digit-1 barrier.
+    const int nw = (m + 31) >> 5;                 // <= kSmMaxKeys / 32 = 1536 words
+    uint32_t* s_g = s_hist0;
+    uint32_t* s_e = s_hist0 + kSmMaxKeys / 32;
     for (int q = warp; q < nw; q += kSmWarps) {
       const int i = 32 * q + lane;
-      const uint32_t key = i < n ? s_keys[i] : 0u;
-      const uint32_t gm = __ballot_sync(0xffffffffu, i < n && key > prefix);
-      const uint32_t em = __ballot_sync(0xffffffffu, i < n && key == prefix);
+      const uint32_t key = i < m ? s_keys[i] : 0u;
+      const uint32_t gm = __ballot_sync(0xffffffffu, i < m && key > prefix);
+      const uint32_t em = __ballot_sync(0xffffffffu, i < m && key == prefix);
       if (lane == 0) { s_g[q] = gm; s_e[q] = em; }
     }
     __syncthreads();
@@ -379,6 +413,16 @@ __global__ void __launch_bounds__(kSmThreads) topk_smem_kernel(const TopkDev a) 
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
     before += inc - own;
+    if constexpr (NCTA > 1) {
+      if (tid == 0) {
+        uint64_t tot = 0;
+        for (int v = 0; v < kSmWarps; ++v) tot += s_wcnt[v];
+        s_cnt = tot;
+      }
+      cg::cluster_group cluster = cg::this_cluster();
+      cluster.sync();
+      for (int r = 0; r < rank; ++r) before += *cluster.map_shared_rank(&s_cnt, r);
+    }
     uint32_t gtb = (uint32_t)(before >> 32), eqb = (uint32_t)(before & 0xffffffffu);
     for (int q = q0; q < q1; ++q) {
       const uint32_t gm = s_g[q], em = s_e[q];
@@ -393,17 +437,20 @@ __global__ void __launch_bounds__(kSmThreads) topk_smem_kernel(const TopkDev a) 
       int64_t pos = (int64_t)gtb + min(eqb, krem);
       while (sel) {
         const int bit = __ffs(sel) - 1;
-        put(a, j, pos++, 32 * q + bit);
+        put(a, j, pos++, lo + 32 * q + bit);
         sel &= sel - 1;
       }
       gtb += __popc(gm);
       eqb += __popc(em);
     }
   } else if (K == n) {
-    for (int t = tid; t < n; t += kSmThreads) put(a, j, t, t);
+    for (int t = lo + tid; t < lo + m; t += kSmThreads) put(a, j, t, t);
   }
-  for (int64_t i = tid; i < w; i += kSmThreads) put(a, j, K + i, n + i);
-  if (a.counts && tid == 0) a.counts[j] = (int32_t)(K + w);
+  if (rank == 0) {
+    for (int64_t i = tid; i < w; i += kSmThreads) put(a, j, K + i, n + i);
+    if (a.counts && tid == 0) a.counts[j] = (int32_t)(K + w);
+  }
+  if constexpr (NCTA > 1) cg::this_cluster().sync();  // no CTA leaves while its peer may read its memory
 }
 
 // ---------------------------------------------------------------------------------------
@@ -621,12 +668,31 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
   // sums several rows over many tokens and there are few selections, the 8-CTA cluster spreads
   // that load over 8 SMs per selection instead.
   const bool wide_load = d->rows_per_sel >= 4 && n_max >= 8192 && (int64_t)d->num_sel * kTcCtas <= 2 * num_sms();
-  if (n_max <= kSmMaxKeys && !wide_load) {
-    int rc = ensure_smem_limit((const void*)topk_smem_kernel, kSmMaxKeys * (int)sizeof(uint32_t), "mskv_topk");
+  if (n_max <= 2 * (int64_t)kSmMaxKeys && !wide_load) {
+    // one CTA per selection, or a 2-CTA cluster beyond kSmMaxKeys candidates
+    const int ncta = n_max <= kSmMaxKeys ? 1 : 2;
+    const int64_t per_cta = (n_max + ncta - 1) / ncta;
+    const size_t smem = (size_t)((per_cta + 3) / 4 * 4 + (per_cta == 0 ? 4 : 0)) * sizeof(uint32_t);
+    const void* kern = ncta == 1 ? (const void*)topk_smem_kernel<1> : (const void*)topk_smem_kernel<2>;
+    int rc = ensure_smem_limit(kern, kSmMaxKeys * (int)sizeof(uint32_t), "mskv_topk");
     if (rc) return rc;
-    const size_t smem = (size_t)((n_max + 3) / 4 * 4 + (n_max == 0 ? 4 : 0)) * sizeof(uint32_t);  // whole 4-key units
-    const cudaError_t e = launch_dependent(topk_smem_kernel, dim3((unsigned)d->num_sel), dim3(kSmThreads), smem,
-                                           as_stream(stream), a);
+    if ((int64_t)d->num_sel * ncta > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "mskv_topk: grid too large");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(d->num_sel * ncta));
+    cfg.blockDim = dim3(kSmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = ncta;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = ncta == 1 ? 1 : 2;      // the one-CTA kernel is launched without a cluster
+    const cudaError_t e = ncta == 1 ? cudaLaunchKernelEx(&cfg, topk_smem_kernel<1>, a)
+                                    : cudaLaunchKernelEx(&cfg, topk_smem_kernel<2>, a);
     if (e != cudaSuccess) return cuda_status(e, "mskv_topk launch");
     return after_launch("mskv_topk");
   }

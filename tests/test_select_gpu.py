@@ -171,7 +171,7 @@ def test_scores_strided_rows(built_lib):
         _assert_scores_close(out.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("T", [40000, 100000, 140000])   # shared-memory CTA, 8-CTA cluster, L2 re-read
+@pytest.mark.parametrize("T", [40000, 70000, 100000, 140000])   # 1 CTA, 2-CTA cluster, 8-CTA cluster, L2 re-read
 def test_topk_paths_ties_nan_ragged(built_lib, T):
     """Each top-k path with quantised (tie-heavy) scores, NaN, ragged lengths and per-sequence k."""
     from mserve_b200 import ops
