@@ -1,0 +1,48 @@
+"""Host-side logic that needs no GPU: decode-step chunking, workload lengths, gathered bytes."""
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+
+
+def test_chunk_bounds_first_chunk_single_sequence():
+    from mserve_b200.engine import OffloadKV
+    cb = lambda B, n: OffloadKV.chunk_bounds(SimpleNamespace(B=B), n).tolist()
+    assert cb(8, 4) == [0, 1, 3, 5, 8]
+    assert cb(8, 1) == [0, 8]
+    assert cb(3, 4) == [0, 1, 2, 3]
+    assert cb(1, 4) == [0, 1]
+    assert cb(32, 4) == [0, 1, 11, 21, 32]
+    for B in range(1, 40):
+        for n in range(1, 9):
+            b = cb(B, n)
+            assert b[0] == 0 and b[-1] == B and all(x < y for x, y in zip(b, b[1:]))
+            assert len(b) - 1 == min(n, B)
+            if min(n, B) > 1:
+                assert b[1] == 1                     # the first chunk holds one sequence
+
+
+def test_chunk_bounds_explicit_sizes():
+    from mserve_b200.engine import OffloadKV
+    eng = SimpleNamespace(B=8)
+    assert OffloadKV.chunk_bounds(eng, [1, 3, 3, 1]).tolist() == [0, 1, 4, 7, 8]
+    for bad in ([1, 2], [0, 8], [4, 5], []):
+        with pytest.raises(ValueError):
+            OffloadKV.chunk_bounds(eng, bad)
+
+
+def test_workload_lengths_and_gathered_bytes():
+    import bench
+    wl = dict(bench.WORKLOADS["llava34b"][0])
+    lens = bench.workload_lens(wl)
+    assert len(lens) == 32 and all(4096 <= x <= 65536 for x in lens)
+    assert lens == bench.workload_lens(wl)           # seeded
+    assert bench.workload_lens(dict(bench.WORKLOADS["qwen7b"][0])) == [16384] * 8
+    # per segment: min(k_b, L_b - R) top-k rows + min(R, L_b) window rows, K and V, 2 bytes
+    eng = SimpleNamespace(len_h=np.array([100, 5, 0]), recent=8, top_k_ratio=None, top_k=50, B=3, Hkv=2,
+                          D=4, topk_h=None, dtype=__import__("torch").bfloat16)
+    rows = (50 + 8) + (0 + 5) + 0
+    assert bench.gathered_bytes(eng) == 2 * rows * 2 * 4 * 2
+    eng.top_k_ratio, eng.topk_h = 0.1, np.array([10, 1, 0])
+    rows = (10 + 8) + (0 + 5) + 0
+    assert bench.gathered_bytes(eng) == 2 * rows * 2 * 4 * 2
