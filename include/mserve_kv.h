@@ -215,9 +215,9 @@ int mskv_score(const mskv_score_desc* d, void* stream);
  * [n, L).  The output row idx[j*out_stride ...] is sorted ascending and holds
  * count = k + (L - n) entries; counts[j] receives it (may be NULL).  Scores of the
  * candidates only are read.  When len != NULL, len_scalar bounds every len[b] (larger values
- * are clamped to it) and sizes the kernel: up to 49152 candidates one 1024-thread CTA per
- * selection keeps the keys in shared memory; up to 131072 a cluster of 8 CTAs does; beyond
- * that one CTA per selection re-reads them from L2. */
+ * are clamped to it) and sizes the kernel: up to 8 x 49152 candidates the keys of a selection
+ * live in shared memory (one 1024-thread CTA up to 49152, else a cluster of 2, 4 or 8 CTAs);
+ * beyond that one CTA per selection re-reads them from L2. */
 typedef struct mskv_topk_desc {
   const float* scores;
   int64_t scores_stride;

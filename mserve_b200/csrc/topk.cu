@@ -1,20 +1,21 @@
 // Top-k token selection with a recent window (mskv_topk).
 //
 // Replaces torch.topk over the head-averaged scores (qwen-eljrte/Qwen_Transformer/
-// attention.py:567-572) with a per-selection radix select:
+// attention.py:567-572) with an exact radix select per selection (one (sequence, KV head) pair
+// in per-head mode, one sequence in the reference's head-averaged mode):
 //
-//  * one 1024-thread CTA per selection (one (sequence, KV head) pair in per-head mode, one
-//    sequence in the reference's head-averaged mode);
-//  * fp32 keys are mapped to order-preserving uint32 (sign flip), and four 8-bit radix
-//    passes over the candidates build a 256-bin histogram of the digit under the current
-//    prefix.  Threads with equal digits are merged with __match_any_sync before one shared
-//    atomic per group, because the high digits of real scores fall into a handful of bins;
-//  * the pass ends knowing the exact k-th key tau and how many keys equal to tau to keep;
-//  * an ordered compaction (each thread owns a contiguous run, one block-wide 64-bit scan
-//    of (#greater, #equal)) writes the selected token indices in ascending order, keeping
-//    ties at tau toward the lower token index, and appends the recent window.  NaN keys
-//    rank highest.
-// The scores are re-read from L2 on every pass (64 KB per 16k-token selection).
+//  * fp32 keys (the selection's score rows summed in row order, scaled) map to order-preserving
+//    uint32 (sign flip; every NaN maps to the largest key);
+//  * the keys live in shared memory: one 1024-thread CTA per selection, or a cluster of 2, 4 or
+//    8 CTAs each holding a share, for up to 8 x 48K candidates;
+//  * digits of 12, 12 and 8 bits: the first histogram is built while the keys load, the next
+//    two passes only compare and count the keys still matching; cluster CTAs sum their
+//    histograms through distributed shared memory; each digit search is a block suffix scan;
+//  * the pass ends knowing the exact k-th key and how many keys equal to it to keep; an ordered
+//    compaction through bitmaps (a ballot pair per 32 keys, a block scan over the words) writes
+//    the selected token indices in ascending order, keeping ties at the threshold toward the
+//    lower token index, and appends the recent window.
+// Beyond 8 x 48K candidates one CTA per selection re-reads the scores from L2 on every pass.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -225,8 +226,8 @@ __global__ void __launch_bounds__(kTkThreads) topk_kernel(const TopkDev a) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Shared-memory path (up to kSmMaxKeys candidates per CTA): one 1024-thread CTA per selection
-// (two, as a cluster, up to 2 x kSmMaxKeys) keeps every candidate key in shared memory.
+// Shared-memory path (up to kSmMaxKeys candidates per CTA): one 1024-thread CTA per selection,
+// or a cluster of 2, 4 or 8 such CTAs, keeps every candidate key in shared memory.
 //
 // Digits of 12, 12 and 8 bits: the first pass histograms every key into 4096 bins (plain
 // shared atomics; a 12-bit digit of an fp32 key spans an eighth of a binade, so real scores
@@ -237,12 +238,6 @@ constexpr int kSmThreads = 1024;
 constexpr int kSmWarps = kSmThreads / 32;
 constexpr int kSmMaxKeys = 48 * 1024;  // a multiple of 4: the buffer holds whole 4-key units
 constexpr int kSmBins = 4096;
-
-__device__ __forceinline__ uint32_t lanemask_lt_sm() {
-  uint32_t m;
-  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
-  return m;
-}
 
 // Finds the bin holding the krem-th largest key of the histogram (bins ordered by value);
 // sets *prefix |= bin << shift and *krem to the rank within that bin.  Every thread calls it.
@@ -314,7 +309,7 @@ __device__ __forceinline__ void cta_group_sync() {
   else __syncthreads();
 }
 
-// One selection per NCTA CTAs (NCTA = 1, or a 2-CTA cluster for up to 2 x kSmMaxKeys
+// One selection per NCTA CTAs (NCTA = 1, or a cluster of 2, 4 or 8 for up to NCTA x kSmMaxKeys
 // candidates): CTA r holds the keys [r*chunk, (r+1)*chunk) in shared memory.  Every radix pass
 // has its own histogram buffer, so no buffer is cleared while the peer CTA may still read it.
 template <int NCTA>
@@ -662,21 +657,42 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
   a.row_block = d->row_block > 0 ? d->row_block : d->rows_per_sel;
   a.sel_stride = d->sel_stride > 0 ? d->sel_stride : (int64_t)d->rows_per_sel * d->scores_stride;
   a.block_stride = d->block_stride;
-  // len_scalar bounds every len[b]; it sizes the per-CTA key buffer of the cluster path.
+  // len_scalar bounds every len[b]; it sizes the per-CTA key buffers.
   const int64_t n_max = d->len_scalar > d->recent ? (int64_t)d->len_scalar - d->recent : 0;
-  // One CTA per selection reads rows_per_sel x n scores through one SM.  When each selection
-  // sums several rows over many tokens and there are few selections, the 8-CTA cluster spreads
-  // that load over 8 SMs per selection instead.
+  // Which kernel (all measured on the decode shapes):
+  //  * up to 2 x kSmMaxKeys candidates: the shared-memory kernel, one CTA per selection, or a
+  //    2-CTA cluster beyond kSmMaxKeys;
+  //  * few selections that each sum several rows over many tokens (a head-averaged selection),
+  //    or up to 8 x kTcMaxKeys candidates: the 8-CTA cluster kernel (one CTA per selection would
+  //    stream rows x tokens x 4 bytes through a single SM; the shared-memory kernel split eight
+  //    ways spends more on its 4096-bin histograms than it saves);
+  //  * longer contexts, up to 8 x kSmMaxKeys: the shared-memory kernel as a 4- or 8-CTA cluster;
+  //  * beyond that: one CTA per selection re-reading the scores from L2.
   const bool wide_load = d->rows_per_sel >= 4 && n_max >= 8192 && (int64_t)d->num_sel * kTcCtas <= 2 * num_sms();
-  if (n_max <= 2 * (int64_t)kSmMaxKeys && !wide_load) {
-    // one CTA per selection, or a 2-CTA cluster beyond kSmMaxKeys candidates
-    const int ncta = n_max <= kSmMaxKeys ? 1 : 2;
+  const int64_t keys_per_cta = (n_max + kTcCtas - 1) / kTcCtas;
+  const bool cluster_path = keys_per_cta <= kTcMaxKeys && (wide_load || n_max > 2 * (int64_t)kSmMaxKeys);
+  int ncta = 0;
+  if (!cluster_path)
+    for (int c : {1, 2, 4, 8})
+      if (!ncta && (n_max + c - 1) / c <= kSmMaxKeys) ncta = c;
+  if (cluster_path && (int64_t)d->num_sel * kTcCtas <= 0x7fffffffLL) {
+    int rc = ensure_smem_limit((const void*)topk_cluster_kernel, 3 * kTcMaxKeys * (int)sizeof(uint32_t), "mskv_topk");
+    if (rc) return rc;
+    const int cap = (int)(keys_per_cta > 0 ? keys_per_cta : 1);
+    const size_t smem = 3 * (size_t)cap * sizeof(uint32_t);
+    const cudaError_t e = launch_dependent(topk_cluster_kernel, dim3((unsigned)(d->num_sel * kTcCtas)),
+                                           dim3(kTcThreads), smem, as_stream(stream), a, cap);
+    if (e != cudaSuccess) return cuda_status(e, "mskv_topk launch");
+    return after_launch("mskv_topk");
+  }
+  if (ncta && (int64_t)d->num_sel * ncta <= 0x7fffffffLL) {
     const int64_t per_cta = (n_max + ncta - 1) / ncta;
     const size_t smem = (size_t)((per_cta + 3) / 4 * 4 + (per_cta == 0 ? 4 : 0)) * sizeof(uint32_t);
-    const void* kern = ncta == 1 ? (const void*)topk_smem_kernel<1> : (const void*)topk_smem_kernel<2>;
+    const void* kern = ncta == 1 ? (const void*)topk_smem_kernel<1>
+                     : ncta == 2 ? (const void*)topk_smem_kernel<2>
+                     : ncta == 4 ? (const void*)topk_smem_kernel<4> : (const void*)topk_smem_kernel<8>;
     int rc = ensure_smem_limit(kern, kSmMaxKeys * (int)sizeof(uint32_t), "mskv_topk");
     if (rc) return rc;
-    if ((int64_t)d->num_sel * ncta > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "mskv_topk: grid too large");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(d->num_sel * ncta));
     cfg.blockDim = dim3(kSmThreads);
@@ -691,22 +707,17 @@ extern "C" int mskv_topk(const mskv_topk_desc* d, void* stream) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = ncta == 1 ? 1 : 2;      // the one-CTA kernel is launched without a cluster
-    const cudaError_t e = ncta == 1 ? cudaLaunchKernelEx(&cfg, topk_smem_kernel<1>, a)
-                                    : cudaLaunchKernelEx(&cfg, topk_smem_kernel<2>, a);
+    cudaError_t e;
+    switch (ncta) {
+      case 1: e = cudaLaunchKernelEx(&cfg, topk_smem_kernel<1>, a); break;
+      case 2: e = cudaLaunchKernelEx(&cfg, topk_smem_kernel<2>, a); break;
+      case 4: e = cudaLaunchKernelEx(&cfg, topk_smem_kernel<4>, a); break;
+      default: e = cudaLaunchKernelEx(&cfg, topk_smem_kernel<8>, a); break;
+    }
     if (e != cudaSuccess) return cuda_status(e, "mskv_topk launch");
     return after_launch("mskv_topk");
   }
-  const int64_t keys_per_cta = (n_max + kTcCtas - 1) / kTcCtas;
-  if (keys_per_cta <= kTcMaxKeys && (int64_t)d->num_sel * kTcCtas <= 0x7fffffffLL) {
-    int rc = ensure_smem_limit((const void*)topk_cluster_kernel, 3 * kTcMaxKeys * (int)sizeof(uint32_t), "mskv_topk");
-    if (rc) return rc;
-    const int cap = (int)(keys_per_cta > 0 ? keys_per_cta : 1);
-    const size_t smem = 3 * (size_t)cap * sizeof(uint32_t);
-    const cudaError_t e = launch_dependent(topk_cluster_kernel, dim3((unsigned)(d->num_sel * kTcCtas)),
-                                           dim3(kTcThreads), smem, as_stream(stream), a, cap);
-    if (e != cudaSuccess) return cuda_status(e, "mskv_topk launch");
-    return after_launch("mskv_topk");
-  }
+  // beyond 8 x kSmMaxKeys candidates: one CTA per selection re-reading the scores from L2
   const cudaError_t e = launch_dependent(topk_kernel, dim3((unsigned)d->num_sel), dim3(kTkThreads), 0,
                                          as_stream(stream), a);
   if (e != cudaSuccess) return cuda_status(e, "mskv_topk launch");

@@ -144,8 +144,8 @@ def test_compute_token_importance_reference_golden(built_lib, golden, case):
         _tie_tolerant_equal(got2[b], ref2[b], scores[b], rtol)
 
 
-def test_topk_beyond_cluster_capacity(built_lib):
-    """More than 8 x 16384 candidates: the single-CTA path re-reading scores from L2."""
+def test_topk_long_context_140k(built_lib):
+    """140K candidates: a 4-CTA cluster holding the keys in shared memory."""
     from mserve_b200 import ops
     g = torch.Generator().manual_seed(21)
     rows = torch.randn(3, 140000, generator=g)
@@ -171,7 +171,7 @@ def test_scores_strided_rows(built_lib):
         _assert_scores_close(out.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("T", [40000, 70000, 100000, 140000])   # 1 CTA, 2-CTA cluster, 8-CTA cluster, L2 re-read
+@pytest.mark.parametrize("T", [40000, 70000, 100000, 200000, 400000])   # 1, 2, 4, 8 CTAs; L2 re-read
 def test_topk_paths_ties_nan_ragged(built_lib, T):
     """Each top-k path with quantised (tie-heavy) scores, NaN, ragged lengths and per-sequence k."""
     from mserve_b200 import ops
