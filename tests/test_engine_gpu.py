@@ -98,3 +98,45 @@ def test_pipelined_step_and_graph_match_per_layer(built_lib, chunks):
     assert torch.equal(out, ref)
     from mserve_b200 import ops
     ops.check_status(torch.device("cuda"))
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.float16, 128), (torch.bfloat16, 64), (torch.float16, 64)])
+def test_decode_layer_dtypes_and_head_dims(built_lib, dtype, D):
+    """The whole decode layer with fp16 keys/values and with head_dim 64 (the 16-bit streaming
+    score path and the tensor-core attention path at both sizes) against the oracle."""
+    from mserve_b200.engine import OffloadKV
+    B, Hq, Hkv, T, K, R = 3, 16, 4, 3000, 300, 32
+    g = torch.Generator().manual_seed(D + (1 if dtype == torch.float16 else 0))
+    eng = OffloadKV(1, B, Hq, Hkv, D, T + 16, top_k=K, recent=R, dtype=dtype)
+    lens = [3000, 2047, 1000]
+    eng.reserve(lens)
+    k = torch.randn(B, Hkv, T, D, generator=g).to(dtype)
+    v = torch.randn(B, Hkv, T, D, generator=g).to(dtype)
+    eng.append_layer(0, k.cuda(), v.cuda())
+    eng.commit()
+    q = torch.randn(B, Hq, D, generator=g).to(dtype)
+    out = eng.decode_layer(0, q.cuda())
+    torch.cuda.synchronize()
+    bufs = eng.buffers()
+    scores, idx, cnt = bufs.scores.cpu().numpy(), bufs.idx.cpu().numpy(), bufs.counts.cpu().numpy()
+    kn, vn = k.float().numpy(), v.float().numpy()
+    ref_scores = ko.gqa_scores(q.float().numpy(), kn, lens=np.asarray(lens))
+    for b in range(B):
+        L = lens[b]
+        s, r = scores[b, :, :L].astype(np.float64), ref_scores[b, :, :L]
+        assert (np.abs(s - r) / (np.abs(r) + np.abs(r).mean())).max() < 1e-3
+    sel, rcnt = ko.select_topk_window(scores.reshape(B * Hkv, -1), top_k=K, recent=R, lens=np.asarray(lens),
+                                      sel_per_batch=Hkv)
+    np.testing.assert_array_equal(cnt, rcnt)
+    kb, hk = to_numpy_bits(bufs.k_sel), to_numpy_bits(k)
+    k_sel = np.zeros((B, Hkv, bufs.k_sel.shape[2], D))
+    v_sel = np.zeros_like(k_sel)
+    for j in range(B * Hkv):
+        b, h = divmod(j, Hkv)
+        np.testing.assert_array_equal(idx[j, :cnt[j]], sel[j])
+        np.testing.assert_array_equal(kb[b, h, :cnt[j]], hk[b, h, sel[j]])
+        k_sel[b, h, :cnt[j]] = kn[b, h, sel[j]]
+        v_sel[b, h, :cnt[j]] = vn[b, h, sel[j]]
+    ref = ko.sparse_sdpa_attention(q.double().numpy()[:, :, None, :], k_sel, v_sel, counts=cnt.reshape(B, Hkv))
+    o = out.float().cpu().numpy()
+    assert np.abs(o - ref).max() / np.abs(ref).max() < 2e-2
