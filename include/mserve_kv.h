@@ -178,11 +178,14 @@ int mskv_copy_rows(const mskv_copy_desc* d, void* stream);
  * method 1 (norm):            scores[b,hk,t] = sqrt(sum_d k[b,hk,t,d]^2) in fp32
  * k rows are addressed by `k` (mskv_rows, base_v unused); q row (b, hq) is at
  * q + b*q_stride_b + hq*q_stride_h (bytes); scores row (b,hk) at
- * scores + (b*kv_heads + hk)*scores_stride (elements); tokens t >= len[b] are not written;
- * tokens whose page is unmapped score -inf (MSKV_STATUS_BAD_PAGE).
- * Fast path (16-bit K, head_dim in {64,128,256}, rows contiguous, page_size dividing 128):
- * a persistent kernel streams 128-token key tiles into shared memory with bulk copies
- * (3-4 stages in flight); other shapes use register-streaming or generic kernels. */
+ * scores + (b*kv_heads + hk)*scores_stride (elements); tokens t >= len[b] are not written
+ * (len[b] above max_tokens is clamped to it); tokens whose page is unmapped score -inf
+ * (MSKV_STATUS_BAD_PAGE).
+ * Fast path (16-bit K, head_dim in {64,128,256}, 16-byte aligned rows, page_size a multiple
+ * of 8): register streaming, 8 rows per group of head_dim/8 lanes with 16-byte loads,
+ * double-buffered so the next slice's loads are in flight while a slice is scored; warps share
+ * the slices that hold tokens equally however ragged len[] is.  Other shapes use a 32-row
+ * register kernel or a generic one. */
 typedef struct mskv_score_desc {
   mskv_rows k;
   const void* q;
@@ -190,7 +193,7 @@ typedef struct mskv_score_desc {
   int64_t q_stride_h;
   float* scores;
   int64_t scores_stride;
-  int64_t max_tokens;           /* upper bound of len[b] (grid size)                  */
+  int64_t max_tokens;           /* upper bound of len[b] (< 2^31), <= scores_stride   */
   uint32_t* status;             /* optional device status word                        */
   int32_t dtype;                /* MSKV_DT_BF16 / F16 / F32, same for q and k         */
   int32_t method;               /* 0 attention_score, 1 norm                          */
