@@ -434,7 +434,7 @@ def run_mserve(args, world, rank, local):
     key_bytes_layer = int(eng.len_h.sum()) * eng.Hkv * eng.D * 2
     stream = torch.cuda.current_stream(dev)
 
-    # The product path: the whole decode step (all layers, chunk-pipelined over three streams)
+    # The product path: the whole decode step (all layers, chunk-pipelined over four streams)
     # captured once as a CUDA graph and replayed.
     out_all = torch.empty((L,) + tuple(bufs.out.shape), dtype=bufs.out.dtype, device=dev)
     n0 = _lib.launch_count()

@@ -2,10 +2,12 @@
 // mskv_gather) and the contiguous row copies behind the paged append and the host write-back
 // (mskv_copy_rows).
 //
-// Design (B200): one CTA owns a tile of rows of one (b, h) segment.  The first threads
-// resolve the tile's source/destination byte offsets (index list, ring, page table, bounds)
-// into shared memory once per row; then all 256 threads stream the tile as VEC-byte chunks
-// with UNROLL independent loads in flight per thread for K and for V before any store.
+// Design (B200): the work is tiles of rows of one (b, h) segment; a CTA takes tiles in a
+// grid-stride loop (a bounded grid for moves that touch host memory, see launch_move).  For
+// each tile the first threads resolve the source/destination byte offsets (index list, ring,
+// page table, bounds) into shared memory once per row; then all 256 threads stream the tile
+// as VEC-byte chunks with UNROLL independent loads in flight per thread for K and for V
+// before any store.
 // Consecutive threads take consecutive 16-byte chunks of a row, so one half-warp reads one
 // 256-byte bf16 row (two aligned 128-byte PCIe read requests) and the stores to HBM are
 // fully coalesced.  Rows that are invalid (index out of range, unmapped page) are skipped

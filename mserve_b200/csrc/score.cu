@@ -194,13 +194,13 @@ __global__ void __launch_bounds__(256) score_fast_kernel(const ScoreDev a) {
 // Main path for 16-bit keys: register streaming, 8 rows per lane group.
 //
 // GL = D/8 lanes own one row (one 16-byte chunk each); a group of GL lanes takes 8
-// consecutive rows per iteration, so every lane keeps exactly 8 independent 16-byte loads in
-// flight (ld.global.nc with L1 bypass and a 256-byte L2 prefetch: one bf16 row) and the
-// kernel stays at <= 64 registers, i.e. 32+ resident warps per SM and ~128 KB of key bytes in
-// flight per SM.  Products use packed fp32x2 FMAs (two lanes of fp32 per instruction); the
-// 8 partial dots are reduce-scattered over 8 lanes and finished with xor-shuffles.
-// (A shared-memory bulk-copy pipeline was measured slower: shared memory caps it at ~8
-// resident warps per SM, too few to hide the per-row arithmetic latency.)
+// consecutive rows per slice, so every lane issues 8 independent 16-byte loads per slice
+// (ld.global.nc with L1 bypass and a 256-byte L2 prefetch: one bf16 row), and a second
+// register buffer keeps the next slice's loads in flight while a slice is scored: 128
+// registers, 2 CTAs (16 warps) and up to 128 KB of key bytes in flight per SM.  Products use
+// packed fp32x2 FMAs (two lanes of fp32 per instruction); the 8 partial dots are
+// reduce-scattered over 8 lanes and finished with xor-shuffles.  (Staging the keys in shared
+// memory -- bulk copies, or cp.async with 1.5x the bytes in flight -- measured no faster.)
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"

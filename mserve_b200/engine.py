@@ -18,6 +18,8 @@ Decode step, per layer (``decode_layer``): GQA-summed fp32 scores from the HBM p
 (mskv_score) -> top-k of [0, L-R) plus the recent window [L-R, L) per (sequence, KV head)
 (mskv_topk) -> gather of the selected K/V rows from the host store into HBM
 (mskv_gather) -> attention over them (mskv_sparse_attention).  No host synchronisation.
+``decode_step`` pipelines these over sequence chunks and four streams and prefetches each
+layer's recent-window rows; ``capture_decode_step`` captures the whole step as a CUDA graph.
 """
 from __future__ import annotations
 
