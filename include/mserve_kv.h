@@ -304,6 +304,40 @@ int mskv_sparse_attention(const mskv_attn_desc* d, void* stream);
 #define MSKV_NOALLOC_ATTN_SCRATCH_BYTES (8u << 20)
 int mskv_sparse_attention_noalloc(const mskv_attn_desc* d, void* stream);
 
+/* ---- prefill image-token filter ------------------------------------------------------------
+ * Replaces dual_attention_filter (qwen-eljrte/Qwen_Transformer/dual_attention_filter.py:6-103).
+ * attn: the attention probabilities of batch 0, element (h, query r, key c) at
+ *   attn + h*stride_h + r*stride_q + c*stride_k (elements), dtype F32 / F16 / BF16.
+ * Image tokens are the keys [img_start, img_start + img_seq); text tokens are the query rows
+ * [text_start, text_start + text_seq) (the reference: img_start = v_token_start, text_start =
+ * v_token_start + img_seq, text_seq = T - text_start).  Over the block [heads, text, img]:
+ *   hm[i,j] = (sum_h attn[h, text_i, img_j]) / heads      (heads in order, fp32)
+ *   sum_j   = sum_i hm[i,j]  (text rows in order),  max_j = max_i hm[i,j],  total = sum_j sum_j
+ * image token j is dropped when sum_j < total*global_thr and max_j < individual_thr; the kept
+ * ones are written to out_idx (int64, ascending; img_seq entries of room) and their number to
+ * *out_count (device int32).  workspace: mskv_image_filter_workspace_bytes(img_seq) bytes of
+ * device memory (column sums, column maxima, partial totals), 4-byte aligned. */
+typedef struct mskv_filter_desc {
+  const void* attn;
+  int64_t stride_h;
+  int64_t stride_q;
+  int64_t stride_k;
+  int64_t* out_idx;
+  int32_t* out_count;
+  void* workspace;
+  uint64_t workspace_bytes;
+  float global_thr;
+  float individual_thr;
+  int32_t dtype;
+  int32_t heads;
+  int32_t img_start;
+  int32_t img_seq;
+  int32_t text_start;
+  int32_t text_seq;
+} mskv_filter_desc;
+uint64_t mskv_image_filter_workspace_bytes(int32_t img_seq);
+int mskv_image_filter(const mskv_filter_desc* d, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

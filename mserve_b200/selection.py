@@ -3,6 +3,8 @@
 Reference: qwen-eljrte/Qwen_Transformer/attention.py
   * compute_token_importance (532-588)  -> mskv_score + mskv_topk
   * sparse_sdpa_attention (591-641)     -> mskv_sparse_attention
+and qwen-eljrte/Qwen_Transformer/dual_attention_filter.py
+  * dual_attention_filter (6-103)       -> mskv_image_filter
   * repeat_kv (1701-1710)               -> same torch view/reshape (plumbing only; the
                                            kernels here never need repeated heads)
 
@@ -128,3 +130,32 @@ def sparse_sdpa_attention(query: torch.Tensor, key_full: Optional[torch.Tensor],
     if dropout_p > 0:
         out = F.dropout(out, p=dropout_p, training=True)
     return out
+
+
+def dual_attention_filter(attn: torch.Tensor, v_token_start: int, img_seq: int, global_thr: float = 1.0,
+                          individual_thr: float = 0.0, min_keep_ratio: float = 0.35, use_fp16: bool = False):
+    """Image tokens kept by the prefill dual-threshold filter (dual_attention_filter.py:6-103).
+
+    attn: [B, H, T, T] attention probabilities (batch 0 is used, as in the reference).  From the
+    head-averaged text x image block, image token j is dropped when its column sum is below
+    global_thr times the sum of all column sums and its column maximum is below
+    individual_thr.  Returns (important_indices int64 [M] on attn's device, ascending,
+    text_seq = T - img_seq - v_token_start).  min_keep_ratio is accepted and, as in the
+    reference, not applied.  use_fp16 rounds fp32 probabilities to fp16 first, as the
+    reference does; the sums are accumulated in fp32 either way.
+    """
+    if attn.dim() != 4:
+        raise AssertionError("attn must be [B, H, T, T]")
+    B, H, T, _ = attn.shape
+    if B < 1:
+        raise AssertionError("attn has no batch")
+    text_seq = T - img_seq - v_token_start
+    img_start, text_start = v_token_start, v_token_start + img_seq
+    a0 = attn[0]
+    if use_fp16 and a0.dtype == torch.float32:      # only the text x image block is rounded
+        a0 = a0[:, text_start:text_start + text_seq, img_start:img_start + img_seq].half()
+        img_start, text_start = 0, 0
+    idx, count = ops.image_filter(a0, img_start=img_start, img_seq=img_seq, text_start=text_start,
+                                  text_seq=text_seq, global_thr=global_thr, individual_thr=individual_thr)
+    return idx[:int(count.item())], int(text_seq)
+

@@ -351,3 +351,32 @@ def page_writeback(pool_k: np.ndarray, pool_v: np.ndarray, page_table: np.ndarra
             slot = t if ring_start is None else (int(ring_start[b]) + t) % ring_cap
             host_k[b, :, slot] = pool_k[p, :, t % ps]
             host_v[b, :, slot] = pool_v[p, :, t % ps]
+
+
+def dual_attention_filter(attn: np.ndarray, v_token_start: int, img_seq: int, global_thr: float = 1.0,
+                          individual_thr: float = 0.0):
+    """Restates dual_attention_filter (qwen-eljrte/Qwen_Transformer/dual_attention_filter.py:6-103).
+
+    attn [B, H, T, T] (batch 0 used).  block = attn[0, :, text rows, image columns]; head_mean =
+    mean over heads (summed in head order, divided by H, fp32); attn_sum = column sums over the
+    text rows (in row order, fp32); text_max = column maxima; an image token is dropped when
+    attn_sum < attn_sum.sum() * global_thr and text_max < individual_thr (lines 56-70).
+    Returns (kept image-token indices ascending, text_seq, attn_sum, text_max, total) with the
+    grand total in float64.
+    """
+    B, H, T, _ = attn.shape
+    text_seq = T - img_seq - v_token_start
+    img_beg, img_end = v_token_start, v_token_start + img_seq
+    txt_beg, txt_end = img_end, img_end + text_seq
+    block = np.asarray(attn[0, :, txt_beg:txt_end, img_beg:img_end], dtype=np.float32)
+    hs = np.zeros(block.shape[1:], dtype=np.float32)
+    for h in range(H):
+        hs = (hs + block[h]).astype(np.float32)
+    head_mean = (hs / np.float32(H)).astype(np.float32)
+    attn_sum = np.zeros(img_seq, dtype=np.float32)
+    for i in range(text_seq):
+        attn_sum = (attn_sum + head_mean[i]).astype(np.float32)
+    text_max = head_mean.max(axis=0) if text_seq else np.full(img_seq, -np.inf, dtype=np.float32)
+    total = float(attn_sum.astype(np.float64).sum())
+    drop = (attn_sum.astype(np.float64) < total * global_thr) & (text_max < np.float32(individual_thr))
+    return np.nonzero(~drop)[0].astype(np.int64), int(text_seq), attn_sum, text_max, total
