@@ -310,13 +310,16 @@ int mskv_sparse_attention_noalloc(const mskv_attn_desc* d, void* stream);
  *   attn + h*stride_h + r*stride_q + c*stride_k (elements), dtype F32 / F16 / BF16.
  * Image tokens are the keys [img_start, img_start + img_seq); text tokens are the query rows
  * [text_start, text_start + text_seq) (the reference: img_start = v_token_start, text_start =
- * v_token_start + img_seq, text_seq = T - text_start).  Over the block [heads, text, img]:
- *   hm[i,j] = (sum_h attn[h, text_i, img_j]) / heads      (heads in order, fp32)
- *   sum_j   = sum_i hm[i,j]  (text rows in order),  max_j = max_i hm[i,j],  total = sum_j sum_j
- * image token j is dropped when sum_j < total*global_thr and max_j < individual_thr; the kept
- * ones are written to out_idx (int64, ascending; img_seq entries of room) and their number to
- * *out_count (device int32).  workspace: mskv_image_filter_workspace_bytes(img_seq) bytes of
- * device memory (column sums, column maxima, partial totals), 4-byte aligned. */
+ * v_token_start + img_seq, text_seq = T - text_start).  Over the block [heads, text, img], with
+ * stage() the rounding to the stage dtype (the input dtype; F16 for F32 input when round_f16,
+ * which first rounds every element to f16 as the reference's use_fp16 does) and fp32 sums:
+ *   hm[i,j] = stage((sum_h attn[h, text_i, img_j]) / heads)      (heads in order)
+ *   sum_j   = stage(sum_i hm[i,j]),  max_j = max_i hm[i,j],  total = stage(sum_j sum_j)
+ * (text rows in blocks of 32, each summed in order, block sums in order; the total over tiles
+ * of 32 columns the same way).  Image token j is dropped when sum_j < stage(total*global_thr)
+ * and max_j < individual_thr; the kept ones are written to out_idx (int64, ascending; img_seq
+ * entries of room) and their number to *out_count (device int32).  workspace: mskv_image_filter_workspace_bytes(img_seq, text_seq) bytes of device
+ * memory (row-block partials, column sums and maxima, tile totals), 4-byte aligned. */
 typedef struct mskv_filter_desc {
   const void* attn;
   int64_t stride_h;
@@ -334,8 +337,10 @@ typedef struct mskv_filter_desc {
   int32_t img_seq;
   int32_t text_start;
   int32_t text_seq;
+  int32_t round_f16;
+  int32_t pad_;
 } mskv_filter_desc;
-uint64_t mskv_image_filter_workspace_bytes(int32_t img_seq);
+uint64_t mskv_image_filter_workspace_bytes(int32_t img_seq, int32_t text_seq);
 int mskv_image_filter(const mskv_filter_desc* d, void* stream);
 
 #ifdef __cplusplus

@@ -101,6 +101,7 @@ class FilterDesc(C.Structure):
         ("out_idx", _vp), ("out_count", _vp), ("workspace", _vp), ("workspace_bytes", C.c_uint64),
         ("global_thr", C.c_float), ("individual_thr", C.c_float), ("dtype", _i32), ("heads", _i32),
         ("img_start", _i32), ("img_seq", _i32), ("text_start", _i32), ("text_seq", _i32),
+        ("round_f16", _i32), ("pad_", _i32),
     ]
 
 
@@ -122,7 +123,7 @@ SIGNATURES = [
     ("mskv_topk", C.c_int, [C.POINTER(TopkDesc), _vp]),
     ("mskv_attention_workspace_bytes", C.c_uint64, [C.POINTER(AttnDesc)]),
     ("mskv_sparse_attention", C.c_int, [C.POINTER(AttnDesc), _vp]),
-    ("mskv_image_filter_workspace_bytes", C.c_uint64, [_i32]),
+    ("mskv_image_filter_workspace_bytes", C.c_uint64, [_i32, _i32]),
     ("mskv_image_filter", C.c_int, [C.POINTER(FilterDesc), _vp]),
 ]
 

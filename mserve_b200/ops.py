@@ -473,29 +473,35 @@ def sparse_attention(q: torch.Tensor, k_sel: torch.Tensor, v_sel: torch.Tensor, 
 # prefill image-token filter
 # ---------------------------------------------------------------------------------------
 def image_filter(attn0: torch.Tensor, *, img_start: int, img_seq: int, text_start: int, text_seq: int,
-                 global_thr: float, individual_thr: float,
+                 global_thr: float, individual_thr: float, round_f16: bool = False,
                  stream: Optional[torch.cuda.Stream] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Kept image tokens of one attention map (mskv_image_filter).
 
     attn0: [H, Q, K] attention probabilities of one sequence (fp32/fp16/bf16, any strides);
     image tokens are the keys [img_start, +img_seq), text tokens the query rows
-    [text_start, +text_seq).  Returns (idx int64 [img_seq] of which the first count entries
-    are the kept image tokens in ascending order, count int32 [1]), both on attn0's device,
-    without synchronising.
+    [text_start, +text_seq).  round_f16 (fp32 input only) rounds every element to fp16 first and
+    computes the stages in fp16, as the reference's use_fp16 does.  Returns (idx int64
+    [img_seq] of which the first count entries are the kept image tokens in ascending order,
+    count int32 [1]), both on attn0's device, without synchronising.
     """
     if attn0.dim() != 3 or not attn0.is_cuda:
         raise ValueError("attn0 must be a CUDA tensor [H, Q, K]")
     if attn0.dtype not in COMPUTE_DTYPES:
         raise TypeError(f"attention probabilities must be float32/float16/bfloat16, got {attn0.dtype}")
+    if round_f16 and attn0.dtype != torch.float32:
+        raise ValueError("round_f16 applies to float32 probabilities only")
     H, Q, K = attn0.shape
     if (img_start < 0 or img_seq < 0 or text_start < 0 or text_seq <= 0 or img_start + img_seq > K
             or text_start + text_seq > Q):
         raise ValueError(f"image keys [{img_start}, +{img_seq}) / text rows [{text_start}, +{text_seq}) "
                          f"do not fit a [{Q}, {K}] map")
     dev = attn0.device
-    idx = torch.empty(max(img_seq, 1), dtype=torch.int64, device=dev)
-    count = torch.empty(1, dtype=torch.int32, device=dev)
-    ws = torch.empty(max(int(lib().mskv_image_filter_workspace_bytes(img_seq)), 4), dtype=torch.uint8, device=dev)
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    with torch.cuda.stream(s):          # outputs and workspace belong to the launching stream
+        idx = torch.empty(max(img_seq, 1), dtype=torch.int64, device=dev)
+        count = torch.empty(1, dtype=torch.int32, device=dev)
+        ws = torch.empty(max(int(lib().mskv_image_filter_workspace_bytes(img_seq, text_seq)), 4), dtype=torch.uint8,
+                         device=dev)
     d = FilterDesc()
     d.attn = attn0.data_ptr()
     d.stride_h, d.stride_q, d.stride_k = attn0.stride(0), attn0.stride(1), attn0.stride(2)
@@ -505,8 +511,9 @@ def image_filter(attn0: torch.Tensor, *, img_start: int, img_seq: int, text_star
     d.dtype = _DTYPE_CODE[attn0.dtype]
     d.heads, d.img_start, d.img_seq = H, int(img_start), int(img_seq)
     d.text_start, d.text_seq = int(text_start), int(text_seq)
+    d.round_f16 = int(bool(round_f16))
     keep = (attn0, idx, count, ws)
-    check(lib().mskv_image_filter(C.byref(d), _stream_ptr(stream)))
+    check(lib().mskv_image_filter(C.byref(d), _stream_ptr(s)))
     del keep
     return idx, count
 

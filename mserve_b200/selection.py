@@ -141,8 +141,9 @@ def dual_attention_filter(attn: torch.Tensor, v_token_start: int, img_seq: int, 
     global_thr times the sum of all column sums and its column maximum is below
     individual_thr.  Returns (important_indices int64 [M] on attn's device, ascending,
     text_seq = T - img_seq - v_token_start).  min_keep_ratio is accepted and, as in the
-    reference, not applied.  use_fp16 rounds fp32 probabilities to fp16 first, as the
-    reference does; the sums are accumulated in fp32 either way.
+    reference, not applied.  Each stage (head mean, column sums, total, threshold) is rounded to
+    the block's dtype, fp16 when use_fp16 rounds an fp32 block first, as the reference's tensor
+    arithmetic does; the sums accumulate in fp32.
     """
     if attn.dim() != 4:
         raise AssertionError("attn must be [B, H, T, T]")
@@ -150,12 +151,9 @@ def dual_attention_filter(attn: torch.Tensor, v_token_start: int, img_seq: int, 
     if B < 1:
         raise AssertionError("attn has no batch")
     text_seq = T - img_seq - v_token_start
-    img_start, text_start = v_token_start, v_token_start + img_seq
-    a0 = attn[0]
-    if use_fp16 and a0.dtype == torch.float32:      # only the text x image block is rounded
-        a0 = a0[:, text_start:text_start + text_seq, img_start:img_start + img_seq].half()
-        img_start, text_start = 0, 0
-    idx, count = ops.image_filter(a0, img_start=img_start, img_seq=img_seq, text_start=text_start,
-                                  text_seq=text_seq, global_thr=global_thr, individual_thr=individual_thr)
+    idx, count = ops.image_filter(attn[0], img_start=v_token_start, img_seq=img_seq,
+                                  text_start=v_token_start + img_seq, text_seq=text_seq, global_thr=global_thr,
+                                  individual_thr=individual_thr,
+                                  round_f16=bool(use_fp16) and attn.dtype == torch.float32)
     return idx[:int(count.item())], int(text_seq)
 

@@ -353,30 +353,59 @@ def page_writeback(pool_k: np.ndarray, pool_v: np.ndarray, page_table: np.ndarra
             host_v[b, :, slot] = pool_v[p, :, t % ps]
 
 
+def _stage(x, stage: str) -> np.ndarray:
+    """Rounds float32 values to the stage dtype ('f32', 'f16' or 'bf16', nearest even)."""
+    x = np.asarray(x, dtype=np.float32)
+    if stage == "f16":
+        return x.astype(np.float16).astype(np.float32)
+    if stage == "bf16":
+        u = x.view(np.uint32).astype(np.uint64)
+        r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+        return r.astype(np.uint32).view(np.float32)
+    if stage != "f32":
+        raise ValueError(f"unknown stage dtype {stage}")
+    return x
+
+
 def dual_attention_filter(attn: np.ndarray, v_token_start: int, img_seq: int, global_thr: float = 1.0,
-                          individual_thr: float = 0.0):
+                          individual_thr: float = 0.0, stage: str = "f32"):
     """Restates dual_attention_filter (qwen-eljrte/Qwen_Transformer/dual_attention_filter.py:6-103).
 
-    attn [B, H, T, T] (batch 0 used).  block = attn[0, :, text rows, image columns]; head_mean =
-    mean over heads (summed in head order, divided by H, fp32); attn_sum = column sums over the
-    text rows (in row order, fp32); text_max = column maxima; an image token is dropped when
-    attn_sum < attn_sum.sum() * global_thr and text_max < individual_thr (lines 56-70).
-    Returns (kept image-token indices ascending, text_seq, attn_sum, text_max, total) with the
-    grand total in float64.
+    attn [B, H, T, T] (batch 0 used).  block = attn[0, :, text rows, image columns] (lines
+    37-43), rounded to the stage dtype (its .half() when use_fp16, line 47); head_mean = mean
+    over heads (line 50); attn_sum = column sums over the text rows (line 54); text_max =
+    column maxima (line 57); an image token is dropped when attn_sum < attn_sum.sum() *
+    global_thr and text_max < individual_thr (line 62).  As torch tensors of the block's dtype,
+    every stage result is rounded to `stage` ('f32', 'f16' or 'bf16'), the sums accumulating in
+    float32.  The summation order is fixed: heads in order; text rows in blocks of 32, each
+    summed in order and the block sums added in order; the total over tiles of 32 columns the
+    same way.  Returns (kept image-token indices ascending, text_seq,
+    attn_sum, text_max, threshold total * global_thr as a float).
     """
     B, H, T, _ = attn.shape
     text_seq = T - img_seq - v_token_start
     img_beg, img_end = v_token_start, v_token_start + img_seq
     txt_beg, txt_end = img_end, img_end + text_seq
-    block = np.asarray(attn[0, :, txt_beg:txt_end, img_beg:img_end], dtype=np.float32)
+    block = _stage(np.asarray(attn[0, :, txt_beg:txt_end, img_beg:img_end], dtype=np.float32), stage)
     hs = np.zeros(block.shape[1:], dtype=np.float32)
     for h in range(H):
         hs = (hs + block[h]).astype(np.float32)
-    head_mean = (hs / np.float32(H)).astype(np.float32)
-    attn_sum = np.zeros(img_seq, dtype=np.float32)
-    for i in range(text_seq):
-        attn_sum = (attn_sum + head_mean[i]).astype(np.float32)
+    head_mean = _stage(hs / np.float32(H), stage)
+    col = np.zeros(img_seq, dtype=np.float32)
+    for c0 in range(0, text_seq, 32):
+        part = np.zeros(img_seq, dtype=np.float32)
+        for i in range(c0, min(text_seq, c0 + 32)):
+            part = (part + head_mean[i]).astype(np.float32)
+        col = (col + part).astype(np.float32)
+    attn_sum = _stage(col, stage)
     text_max = head_mean.max(axis=0) if text_seq else np.full(img_seq, -np.inf, dtype=np.float32)
-    total = float(attn_sum.astype(np.float64).sum())
-    drop = (attn_sum.astype(np.float64) < total * global_thr) & (text_max < np.float32(individual_thr))
-    return np.nonzero(~drop)[0].astype(np.int64), int(text_seq), attn_sum, text_max, total
+    t = np.float32(0)
+    for t0 in range(0, img_seq, 32):
+        ts = np.float32(0)
+        for c in range(t0, min(img_seq, t0 + 32)):
+            ts = np.float32(ts + attn_sum[c])
+        t = np.float32(t + ts)
+    total = _stage(np.float32(t), stage)
+    thr = _stage(total * np.float32(global_thr), stage)[()]
+    drop = (attn_sum < thr) & (text_max < np.float32(individual_thr))
+    return np.nonzero(~drop)[0].astype(np.int64), int(text_seq), attn_sum, text_max, float(thr)

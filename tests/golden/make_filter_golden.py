@@ -26,6 +26,9 @@ CASES = [  # name, dtype, H, v_token_start, img_seq, text_seq, global_thr, indiv
     ("defaults", torch.float32, 3, 2, 97, 7, 1.0, 0.0, False),
     ("bf16", torch.bfloat16, 4, 8, 200, 24, 0.003, 0.01, False),
     ("fp16_round", torch.float32, 4, 15, 300, 40, 0.002, 0.01, True),
+    # the arguments of the reference's call site (attention.py:1331): v_token_start 15,
+    # global_thr 0.001, individual_thr 0.01; Qwen2.5-VL-7B's 28 heads, a 14 x 14 token image
+    ("callsite", torch.float32, 28, 15, 196, 45, 0.001, 0.01, False),
 ]
 
 
