@@ -14,7 +14,9 @@ the whole step (all ranks), ms_per_step = decode-step time (max over ranks).  Wi
 (torchrun) every rank serves its own 8 sequences over its own host link; there is no
 collective on the data path (weak scaling).  --impl reference times the C restatement of the
 reference's CPU path (oracle/oracle_kv.c: scores, selection, index_select gather + the H2D
-copy of the gathered rows, attention) on the host cores.
+copy of the gathered rows, attention) on the host cores.  The line's decode_loop field times
+the same step in a decode loop that appends each step's token to every layer (begin_step()
+and a step captured with k_new/v_new), so the cache grows as the loop runs.
 """
 from __future__ import annotations
 
@@ -77,6 +79,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (smaller test runs only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode-loop", action="store_true")
     ap.add_argument("--chunks", type=int, default=4, help="sequence chunks pipelined per layer")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen7b",
                     help="qwen7b (the headline workload) or qwen32b (64 layers need ~140 GB of pinned host "
@@ -547,6 +550,48 @@ def run_mserve(args, world, rank, local):
                          "fp32 scores, radix top-k ∪ window, index_select gather, H2D of the gathered rows, attention",
                "ms_per_layer": s * 1e3, "breakdown_ms": reps[-1][1], "cpu": cpu_model()}
 
+    # A decode loop whose step writes its own token into every layer (HBM key page + host
+    # store): begin_step() grows the lengths, then the step captured with k_new/v_new and a
+    # length bound is replayed.  Run last: it grows the cache.
+    loop = None
+    n_loop = min(args.steps, eng.C - int(eng.len_h.max()) - args.warmup - 1)
+    if not args.no_decode_loop and n_loop > 0:
+        B, Hkv, D = eng.B, eng.Hkv, eng.D
+        g2 = torch.Generator(device=dev).manual_seed(3000 + rank)
+        k_new = torch.randn(L, B, Hkv, D, generator=g2, device=dev).to(torch.bfloat16)
+        v_new = torch.randn(L, B, Hkv, D, generator=g2, device=dev).to(torch.bfloat16)
+        t_bound = int(eng.len_h.max()) + args.warmup + n_loop + 1
+        eng.begin_step()
+        n0 = _lib.launch_count()
+        g_loop = eng.capture_decode_step(q, out_all, chunks=args.chunks, k_new=k_new, v_new=v_new,
+                                         t_bound=t_bound)
+        loop_kernels = (_lib.launch_count() - n0) // 2
+        for _ in range(args.warmup):
+            eng.begin_step()
+            g_loop.replay()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        loop_bytes = 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n_loop):
+            eng.begin_step()
+            loop_bytes += gathered_bytes(eng) * L
+            g_loop.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        ops.check_status(dev, "bench decode loop")
+        tl = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+        loop = {"value": sum_over_ranks(loop_bytes, world) / tl / 1e9, "unit": "GB/s",
+                "ms_per_step": tl / n_loop * 1e3, "steps": n_loop, "kernels_per_step": loop_kernels,
+                "tokens_appended_per_step": B * world,
+                "host_write_bytes_per_step": 2 * L * B * Hkv * D * 2 * world,
+                "note": "each step: begin_step() on the host (lengths, splits, new pages through pinned "
+                        "staging), then the captured step, which writes its token into every layer's HBM "
+                        "key page and host store before that layer's selection; CUDA events around the loop"}
+        del g_loop
+
     peaks_json = measured_peaks()
     gather_gbs = gb_layer / (gat_ms * 1e-3) / 1e9
     roofline = {"bound": "host_link", "kernel": "move_rows_kernel (mskv_gather)", "achieved": gather_gbs,
@@ -585,7 +630,7 @@ def run_mserve(args, world, rank, local):
             "gather_frac_of_concurrent_h2d_peak_whole_step": value / peaks_all["h2d_sum"],
             "host_placement": {"numa_node": numa_node, "local_cpus": len(eng.host_cpus),
                                "note": "host store allocated on the GPU's local CPUs (0: placement left to the system)"}, "gather_frac_of_h2d_peak_whole_step": value / world / peaks["h2d"],
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "decode_loop": loop,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

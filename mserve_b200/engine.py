@@ -12,7 +12,10 @@ Storage (per layer):
 
 Append (prefill chunk or decode token), per layer: the new K rows are scattered into their
 HBM pages (mskv_copy_rows, paged destination) and the new K and V rows are written through
-to the host store (mskv_copy_rows, ring destination, zero-copy PCIe stores).
+to the host store (mskv_copy_rows, ring destination, zero-copy PCIe stores).  A decode loop
+appends its own token inside the step: begin_step() grows the lengths without a host
+synchronisation, decode_step(..., k_new, v_new) writes each layer's token before that
+layer's selection, and a step captured with a length bound replays as the cache grows.
 
 Decode step, per layer (``decode_layer``): GQA-summed fp32 scores from the HBM pages
 (mskv_score) -> top-k of [0, L-R) plus the recent window [L-R, L) per (sequence, KV head)
@@ -103,6 +106,14 @@ class OffloadKV:
         self._pending = None
         self._bufs: Optional[DecodeBuffers] = None
         self._sel2 = None
+        # Decode-token appends (begin_step + decode_step with k_new/v_new): the new token's
+        # position per sequence, a count of one per sequence, and pinned staging for the
+        # host-computed lengths, splits, per-sequence k and page table, guarded by an event.
+        self.tok_new = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        self.ones_b = torch.ones(batch, dtype=torch.int32, device=self.device)
+        self._stage = torch.empty(6 * batch, dtype=torch.int32).pin_memory()
+        self._pt_stage = torch.empty(batch, self.max_pages, dtype=torch.int32).pin_memory()
+        self._stage_ev: Optional[torch.cuda.Event] = None
 
     # ------------------------------------------------------------------ append
     def reserve(self, n_new: Sequence[int]) -> None:
@@ -155,18 +166,80 @@ class OffloadKV:
         n_new, tok0, counts = self._pending
         self.len_h = self.len_h + n_new
         self.lens.copy_(torch.from_numpy(self.len_h.astype(np.int32)), non_blocking=False)
+        split = self._refresh_split()
         if self.top_k_ratio is not None:
-            self.topk_h = np.array([math.ceil(self.top_k_ratio * int(n)) for n in self.len_h], dtype=np.int64)
             self.topk_dev.copy_(torch.from_numpy(self.topk_h.astype(np.int32)), non_blocking=False)
-        n = np.maximum(self.len_h - self.recent, 0)
-        k = self.topk_h if self.top_k_ratio is not None else np.full(self.B, self.top_k, dtype=np.int64)
-        split = np.stack([n, np.minimum(k, n), self.len_h - n]).astype(np.int32)
         self.split.copy_(torch.from_numpy(split), non_blocking=False)
         # tok0/counts were read by kernels on the current stream; keep them alive until then.
         cur = torch.cuda.current_stream(self.device)
         tok0.record_stream(cur)
         counts.record_stream(cur)
         self._pending = None
+
+    def _refresh_split(self) -> np.ndarray:
+        """Per-sequence k (top_k_ratio) and the [n_b, k'_b, w_b] split for the host lengths."""
+        if self.top_k_ratio is not None:
+            self.topk_h = np.array([math.ceil(self.top_k_ratio * int(n)) for n in self.len_h], dtype=np.int64)
+        n = np.maximum(self.len_h - self.recent, 0)
+        k = self.topk_h if self.top_k_ratio is not None else np.full(self.B, self.top_k, dtype=np.int64)
+        return np.stack([n, np.minimum(k, n), self.len_h - n]).astype(np.int32)
+
+    def begin_step(self) -> None:
+        """Room for one new token per sequence, for a decode_step given k_new/v_new.
+
+        Maps a page for every sequence whose token starts one, and sets the device-side
+        lengths, selection splits, per-sequence k and the new token's position (tok_new, the
+        length before the step) -- through pinned staging copies on the current stream, with
+        no host synchronisation (the host waits only for the previous step's staging copies).
+        The step then scores and selects over the grown cache, the new token included, as the
+        reference's decode scores over cat(past, new) (qwen-eljrte/Qwen_Transformer/
+        kv_cache.py:631-643); decode_step writes the token itself.
+        """
+        if self._pending is not None:
+            raise RuntimeError("begin_step() inside reserve()/commit()")
+        if (self.len_h + 1 > self.C).any():
+            raise ValueError(f"a decode token exceeds the store capacity of {self.C} tokens per sequence")
+        mapped = False
+        for b in range(self.B):
+            p = int(self.len_h[b]) // self.page_size
+            if self.page_table_h[b, p] < 0:
+                if not self._free:
+                    raise RuntimeError("HBM key-page pool exhausted")
+                self.page_table_h[b, p] = self._free.pop()
+                mapped = True
+        if self._stage_ev is not None:
+            self._stage_ev.synchronize()        # the staging buffers' last copies are done
+        B = self.B
+        old = self.len_h
+        self.len_h = self.len_h + 1
+        split = self._refresh_split()
+        st = self._stage.numpy()
+        st[0:B] = self.len_h
+        st[B:2 * B] = old
+        st[2 * B:5 * B] = split.reshape(-1)
+        st[5 * B:6 * B] = self.topk_h
+        if mapped:
+            self._pt_stage.numpy()[:] = self.page_table_h
+            self.page_table.copy_(self._pt_stage, non_blocking=True)
+        self.lens.copy_(self._stage[0:B], non_blocking=True)
+        self.tok_new.copy_(self._stage[B:2 * B], non_blocking=True)
+        self.split.copy_(self._stage[2 * B:5 * B].view(3, B), non_blocking=True)
+        if self.top_k_ratio is not None:
+            self.topk_dev.copy_(self._stage[5 * B:6 * B], non_blocking=True)
+        self._stage_ev = torch.cuda.Event()
+        self._stage_ev.record(torch.cuda.current_stream(self.device))
+
+    def _append_token(self, layer: int, k_tok: torch.Tensor, v_tok: torch.Tensor) -> None:
+        """The step's token [B, Hkv, D] of one layer: K into its HBM page, K and V written
+        through to the host store, at position tok_new of every sequence (begin_step)."""
+        k4, v4 = k_tok.unsqueeze(2), v_tok.unsqueeze(2)
+        src = ops.strided_rows(k4, v4, device=self.device)
+        src_k_only = ops.strided_rows(k4, None, device=self.device)
+        pages = ops.paged_rows(self.pool_k[layer], None, self.page_table, len_scalar=self.C, tok0=self.tok_new)
+        host = ops.strided_rows(self.host_k[layer], self.host_v[layer], len_scalar=self.C,
+                                ring_start=self.ring_start, ring_cap=self.C, tok0=self.tok_new, device=self.device)
+        ops.copy_rows(src_k_only, pages, batch=self.B, num_tokens=1, counts=self.ones_b, device=self.device)
+        ops.copy_rows(src, host, batch=self.B, num_tokens=1, counts=self.ones_b, device=self.device)
 
     # ------------------------------------------------------------------ decode
     def buffers(self) -> DecodeBuffers:
@@ -193,10 +266,13 @@ class OffloadKV:
                  out=bufs.idx, counts=bufs.counts, k_bound=k_bound)
         return bufs.idx, bufs.counts
 
-    def _top_k(self, b0: int, b1: int):
-        """(top_k argument, host bound) of sequences [b0, b1) for ops.topk."""
+    def _top_k(self, b0: int, b1: int, t_bound: Optional[int] = None):
+        """(top_k argument, host bound) of sequences [b0, b1) for ops.topk; with t_bound the
+        bound covers every length up to t_bound (a step replayed while the cache grows)."""
         if self.top_k_ratio is None:
             return self.top_k, None
+        if t_bound is not None:
+            return self.topk_dev[b0:b1], math.ceil(self.top_k_ratio * int(t_bound))
         return self.topk_dev[b0:b1], int(self.topk_h[b0:b1].max(initial=0))
 
     def gather(self, layer: int, idx: torch.Tensor, counts: torch.Tensor, bufs: Optional[DecodeBuffers] = None):
@@ -265,7 +341,7 @@ class OffloadKV:
         def select():
             keys = ops.paged_rows(self.pool_k[layer], None, self.page_table[b0:b1], len_=lens)
             ops.score(q[b0:b1], keys, batch=nb, kv_heads=Hkv, max_tokens=T, out=scores, method=0)
-            top_k, k_bound = self._top_k(b0, b1)
+            top_k, k_bound = self._top_k(b0, b1, T)
             ops.topk(scores.view(nb * Hkv, C), top_k=top_k, recent=self.recent, len_=lens, len_scalar=T,
                      rows_per_sel=1, sel_per_batch=Hkv, out=idx, counts=counts, k_bound=k_bound)
 
@@ -278,7 +354,9 @@ class OffloadKV:
 
         return select, gather, attend
 
-    def decode_step(self, q_all: torch.Tensor, out_all: torch.Tensor, chunks: int = 4, streams=None) -> None:
+    def decode_step(self, q_all: torch.Tensor, out_all: torch.Tensor, chunks: int = 4, streams=None, *,
+                    k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None,
+                    t_bound: Optional[int] = None) -> None:
         """All layers of one decode step, pipelined over sequence chunks.
 
         q_all: [L, B, Hq, D]; out_all: [L, B, Hq, 1, D]; chunks: a number of equal chunks or
@@ -291,9 +369,26 @@ class OffloadKV:
         the call can be captured in a CUDA graph.  The recent-window rows of layer l+1 (known
         before its query) are copied while layer l finishes, into the second of two alternating
         selected-row buffer sets.  Outputs are bit-identical to decode_layer.
+
+        k_new, v_new: [L, B, Hkv, D], the step's own token of every layer, after begin_step():
+        layer l's token is written (its HBM page and the host store) on the caller's stream
+        before layer l's selection, and before its window rows are copied.  t_bound: the
+        length bound that the kernels are launched for (default: the current longest
+        sequence); a step captured with t_bound >= the current lengths stays valid while
+        begin_step grows them up to t_bound.
         """
         bufs = self.buffers()
         T = int(self.len_h.max(initial=0))
+        if t_bound is not None:
+            if not T <= int(t_bound) <= self.C:
+                raise ValueError(f"t_bound {t_bound} must lie in [{T}, {self.C}]")
+            T = int(t_bound)
+        append = k_new is not None or v_new is not None
+        if append:
+            want = (self.L, self.B, self.Hkv, self.D)
+            if (k_new is None or v_new is None or tuple(k_new.shape) != want or tuple(v_new.shape) != want
+                    or k_new.dtype != self.dtype or v_new.dtype != self.dtype):
+                raise ValueError(f"k_new and v_new must both be {self.dtype} {list(want)}")
         cur = torch.cuda.current_stream(self.device)
         s_g0, s_g1, s_att = streams or self._side_streams()
         gat_streams = (s_g0, s_g1)
@@ -301,6 +396,8 @@ class OffloadKV:
         n_chunks = len(bounds) - 1
         s_win = gat_streams[(n_chunks - 1) % 2]     # the stream of each layer's last gather
         sel_rows = [self._sel_rows(0, bufs), self._sel_rows(1, bufs)]
+        if append:
+            self._append_token(0, k_new[0], v_new[0])
         start = torch.cuda.Event()
         start.record(cur)
         for st in (s_g0, s_g1, s_att):
@@ -332,11 +429,19 @@ class OffloadKV:
                     gat_ev.append(g)
             this_win = win_ev
             if layer + 1 < self.L:
+                # The next layer's token goes in after this layer's selections (so before the
+                # next layer's, on this stream) and before the next layer's window rows move.
+                if append:
+                    self._append_token(layer + 1, k_new[layer + 1], v_new[layer + 1])
+                    app_ev = torch.cuda.Event()
+                    app_ev.record(cur)
                 # The next layer's window rows cross the link while this layer's last attention
                 # and the next layer's first selection run.  Their buffer set was last read by
                 # the attention of layer - 1, which finished before this layer's selections.
                 win_ev = torch.cuda.Event()
                 with torch.cuda.stream(s_win):
+                    if append:
+                        s_win.wait_event(app_ev)
                     self._window_rows(layer + 1, *sel_rows[(layer + 1) % 2])
                     win_ev.record(s_win)
             with torch.cuda.stream(s_att):
@@ -375,18 +480,26 @@ class OffloadKV:
             self._streams = tuple(torch.cuda.Stream(self.device) for _ in range(3))
         return self._streams
 
-    def capture_decode_step(self, q_all: torch.Tensor, out_all: torch.Tensor, chunks: int = 4):
-        """CUDA graph of ``decode_step`` on fixed q/out buffers; returns the graph (``.replay()``).
+    def capture_decode_step(self, q_all: torch.Tensor, out_all: torch.Tensor, chunks: int = 4, *,
+                            k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None,
+                            t_bound: Optional[int] = None):
+        """CUDA graph of ``decode_step`` on fixed q/out (and k_new/v_new) buffers; returns the
+        graph (``.replay()``).
 
         Replaying the graph launches every kernel of the step at once.  The buffers and the
-        engine must stay alive, and the cache must not grow, while the graph is in use.
+        engine must stay alive while the graph is in use, and the lengths must stay within
+        t_bound (default: the current longest sequence, i.e. the cache must not grow).  With
+        k_new/v_new, each replay follows a begin_step() and writes that step's token; the
+        capture itself runs the current step once (its warm-up), and replaying a step again
+        rewrites the same token and recomputes the same outputs.
         """
         side = self._side_streams()
-        self.decode_step(q_all, out_all, chunks, side)      # warm-up: allocates workspaces
+        kw = dict(k_new=k_new, v_new=v_new, t_bound=t_bound)
+        self.decode_step(q_all, out_all, chunks, side, **kw)      # warm-up: allocates workspaces
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, capture_error_mode="relaxed"):
-            self.decode_step(q_all, out_all, chunks, side)
+            self.decode_step(q_all, out_all, chunks, side, **kw)
         return g
 
     # ------------------------------------------------------------------ views for tests / baselines

@@ -140,3 +140,89 @@ def test_decode_layer_dtypes_and_head_dims(built_lib, dtype, D):
     ref = ko.sparse_sdpa_attention(q.double().numpy()[:, :, None, :], k_sel, v_sel, counts=cnt.reshape(B, Hkv))
     o = out.float().cpu().numpy()
     assert np.abs(o - ref).max() / np.abs(ref).max() < 2e-2
+
+
+def _twin_engines(B, Hq, Hkv, D, lens, C, L, seed, **sel):
+    """Two engines holding the same prefilled cache (lengths `lens`)."""
+    from mserve_b200.engine import OffloadKV
+    engs = [OffloadKV(L, B, Hq, Hkv, D, C, **sel) for _ in range(2)]
+    g = torch.Generator().manual_seed(seed)
+    T = max(lens)
+    rows = [(torch.randn(B, Hkv, T, D, generator=g).to(torch.bfloat16).cuda(),
+             torch.randn(B, Hkv, T, D, generator=g).to(torch.bfloat16).cuda()) for _ in range(L)]
+    for eng in engs:
+        eng.reserve(lens)
+        for layer, (k, v) in enumerate(rows):
+            eng.append_layer(layer, k, v)
+        eng.commit()
+    return engs, g
+
+
+@pytest.mark.parametrize("sel", [dict(top_k=64, recent=8), dict(top_k_ratio=0.125, recent=4), dict(top_k=40)])
+def test_decode_loop_appends_its_token_in_the_graph(built_lib, sel):
+    """A decode loop whose step writes its own token: begin_step() then one CUDA graph captured
+    once with a length bound, replayed every step while the cache grows across page
+    boundaries, against the same steps done eagerly (reserve / append_layer / commit, then
+    decode_layer per layer): outputs bit-identical every step; host store and HBM key pages
+    bit-identical at the end."""
+    B, Hq, Hkv, D, L, steps = 5, 16, 4, 128, 3, 21
+    lens = [300, 31, 47, 16, 129]
+    C = max(lens) + steps + 8
+    (eng, ref), g = _twin_engines(B, Hq, Hkv, D, lens, C, L, seed=11, **sel)
+    dev = torch.device("cuda")
+    q = torch.zeros(L, B, Hq, D, dtype=torch.bfloat16, device=dev)
+    kn = torch.zeros(L, B, Hkv, D, dtype=torch.bfloat16, device=dev)
+    vn = torch.zeros_like(kn)
+    out = torch.zeros(L, B, Hq, 1, D, dtype=torch.bfloat16, device=dev)
+    graph = None
+    for step in range(steps):
+        q.copy_(torch.randn(L, B, Hq, D, generator=g).to(torch.bfloat16))
+        kn.copy_(torch.randn(L, B, Hkv, D, generator=g).to(torch.bfloat16))
+        vn.copy_(torch.randn(L, B, Hkv, D, generator=g).to(torch.bfloat16))
+        eng.begin_step()
+        if graph is None:          # the capture runs this step once
+            graph = eng.capture_decode_step(q, out, chunks=3, k_new=kn, v_new=vn, t_bound=C)
+        else:
+            graph.replay()
+        ref.reserve([1] * B)
+        for layer in range(L):
+            ref.append_layer(layer, kn[layer].unsqueeze(2), vn[layer].unsqueeze(2))
+        ref.commit()
+        want = torch.stack([ref.decode_layer(layer, q[layer]).clone() for layer in range(L)])
+        torch.cuda.synchronize()
+        assert torch.equal(out, want), f"step {step}"
+    assert (eng.len_h == ref.len_h).all() and (eng.len_h == np.asarray(lens) + steps).all()
+    assert torch.equal(eng.lens, ref.lens) and torch.equal(eng.split, ref.split)
+    pt = eng.page_table.cpu().numpy()
+    pt_ref = ref.page_table.cpu().numpy()
+    for layer in range(L):
+        for b in range(B):
+            hk, hv = eng.host_logical(layer, b)
+            rk, rv = ref.host_logical(layer, b)
+            assert torch.equal(hk, rk) and torch.equal(hv, rv)
+            n = int(eng.len_h[b])
+            pool, pool_ref = to_numpy_bits(eng.pool_k[layer]), to_numpy_bits(ref.pool_k[layer])
+            mine = np.stack([pool[pt[b, t // 16], :, t % 16] for t in range(n)], axis=1)
+            theirs = np.stack([pool_ref[pt_ref[b, t // 16], :, t % 16] for t in range(n)], axis=1)
+            np.testing.assert_array_equal(mine, theirs)
+    from mserve_b200 import ops
+    ops.check_status(dev)
+
+
+def test_begin_step_guards(built_lib):
+    from mserve_b200.engine import OffloadKV
+    eng = OffloadKV(1, 2, 4, 2, 64, 20, top_k=4, recent=2)
+    eng.reserve([20, 3])
+    k = torch.zeros(2, 2, 20, 64, dtype=torch.bfloat16, device="cuda")
+    eng.append_layer(0, k, k)
+    with pytest.raises(RuntimeError):
+        eng.begin_step()                     # inside reserve()/commit()
+    eng.commit()
+    with pytest.raises(ValueError):
+        eng.begin_step()                     # sequence 0 is full
+    q = torch.zeros(1, 2, 4, 64, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(1, 2, 4, 1, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        eng.decode_step(q, out, k_new=torch.zeros(1, 2, 2, 64, dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(ValueError):
+        eng.decode_step(q, out, t_bound=21)
