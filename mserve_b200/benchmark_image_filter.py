@@ -19,7 +19,7 @@ reset and the kernel): a CUDA graph of 20 x (L2 flush, call) minus a graph of 20
 median over replays, divided by 20; and the HBM roofline: algorithmic bytes = heads x text x
 image x 4 (the block read) over that time.
 
-    python -m mserve_b200.benchmark_image_filter [--reps 30]
+    python -m mserve_b200.benchmark_image_filter [--reps 30] [--graph-calls 20] [--only NAME]
 """
 from __future__ import annotations
 
@@ -104,12 +104,15 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=30)
     ap.add_argument("--graph-calls", type=int, default=20)
+    ap.add_argument("--only", choices=[w[0] for w in WORKLOADS], default=None, help="run one workload")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     peak, peak_kind = hbm_peak_gbs()
     for name, H, start, img, text in WORKLOADS:
+        if args.only and name != args.only:
+            continue
         T = start + img + text
         attn = probabilities(H, T, seed=img + text, dev=dev)
         ours, ts = dual_attention_filter(attn, start, img, GLOBAL_THR, INDIVIDUAL_THR)
