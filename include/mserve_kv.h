@@ -47,8 +47,7 @@ extern "C" {
 #define MSKV_STATUS_INDEX_OOB 0x1u   /* a source token index was outside [0, len)            */
 #define MSKV_STATUS_BAD_PAGE 0x2u    /* a page-table entry needed by a row was negative      */
 #define MSKV_STATUS_DST_OOB 0x4u     /* a destination token was outside [0, len)             */
-#define MSKV_STATUS_TIMEOUT 0x8u     /* reserved for kernels with bounded waits (none wait at */
-                                     /* present: every kernel here runs without spin-waits)   */
+#define MSKV_STATUS_TIMEOUT 0x8u     /* a bounded wait (mskv_flag_wait) reached its time limit */
 
 /* ---- element types ---------------------------------------------------------------------- */
 #define MSKV_DT_F32 0
@@ -203,6 +202,12 @@ typedef struct mskv_score_desc {
   int32_t head_dim;
 } mskv_score_desc;
 int mskv_score(const mskv_score_desc* d, void* stream);
+/* mskv_score that also stores every score into npeers (0..7) other copies of d->scores, at
+ * the same offsets: the score rows of this rank's KV heads written straight into the other
+ * ranks' gathered buffers through CUDA IPC mappings (mskv_ipc_open), over NVLink.  The
+ * kernel makes its stores system-visible before it exits; signal the peers afterwards with
+ * mskv_flag_signal on the same stream. */
+int mskv_score_fanout(const mskv_score_desc* d, float* const* peer_scores, int32_t npeers, void* stream);
 
 /* ---- (b) top-k with recent window ---------------------------------------------------------
  * Replaces the selection half of compute_token_importance
@@ -342,6 +347,25 @@ typedef struct mskv_filter_desc {
 } mskv_filter_desc;
 uint64_t mskv_image_filter_workspace_bytes(int32_t img_seq, int32_t text_seq);
 int mskv_image_filter(const mskv_filter_desc* d, void* stream);
+
+/* ---- peer memory and flags (score-row exchange between the GPUs of one node) --------------
+ * The shared selection's exchange of score rows (attention.py:558-572 with the KV heads on
+ * several GPUs) without a collective library: device memory from mskv_ipc_alloc (zeroed;
+ * `handle` receives mskv_ipc_handle_bytes() bytes, a cudaIpcMemHandle_t) is mapped by the
+ * other processes with mskv_ipc_open and released with mskv_ipc_close / mskv_ipc_free.
+ * mskv_flag_signal stores `value` at flags[r][index] for r < nranks (int64 elements, release
+ * at system scope) once the stream's earlier work is complete; mskv_flag_wait makes the
+ * stream wait until each of flags[0..count) equals `value` (at_least: is >= value), for at
+ * most timeout_ns (0 < timeout <= 60 s), after which it sets MSKV_STATUS_TIMEOUT in `status`
+ * and lets the stream continue.  Neither uses multicast. */
+uint64_t mskv_ipc_handle_bytes(void);
+int mskv_ipc_alloc(uint64_t bytes, void** ptr, void* handle);
+int mskv_ipc_open(const void* handle, void** ptr);
+int mskv_ipc_close(void* ptr);
+int mskv_ipc_free(void* ptr);
+int mskv_flag_signal(int64_t* const* flags, int32_t nranks, int32_t index, int64_t value, void* stream);
+int mskv_flag_wait(const int64_t* flags, int32_t count, int64_t value, int32_t at_least, uint64_t timeout_ns,
+                   uint32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

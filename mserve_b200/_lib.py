@@ -120,11 +120,19 @@ SIGNATURES = [
     ("mskv_gather", C.c_int, [C.POINTER(GatherDesc), _vp]),
     ("mskv_copy_rows", C.c_int, [C.POINTER(CopyDesc), _vp]),
     ("mskv_score", C.c_int, [C.POINTER(ScoreDesc), _vp]),
+    ("mskv_score_fanout", C.c_int, [C.POINTER(ScoreDesc), C.POINTER(_vp), _i32, _vp]),
     ("mskv_topk", C.c_int, [C.POINTER(TopkDesc), _vp]),
     ("mskv_attention_workspace_bytes", C.c_uint64, [C.POINTER(AttnDesc)]),
     ("mskv_sparse_attention", C.c_int, [C.POINTER(AttnDesc), _vp]),
     ("mskv_image_filter_workspace_bytes", C.c_uint64, [_i32, _i32]),
     ("mskv_image_filter", C.c_int, [C.POINTER(FilterDesc), _vp]),
+    ("mskv_ipc_handle_bytes", C.c_uint64, []),
+    ("mskv_ipc_alloc", C.c_int, [C.c_uint64, C.POINTER(_vp), _vp]),
+    ("mskv_ipc_open", C.c_int, [_vp, C.POINTER(_vp)]),
+    ("mskv_ipc_close", C.c_int, [_vp]),
+    ("mskv_ipc_free", C.c_int, [_vp]),
+    ("mskv_flag_signal", C.c_int, [C.POINTER(_vp), _i32, _i32, _i64, _vp]),
+    ("mskv_flag_wait", C.c_int, [_vp, _i32, _i64, _i32, C.c_uint64, _vp, _vp]),
 ]
 
 _lib = None

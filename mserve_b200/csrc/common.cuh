@@ -25,6 +25,9 @@ int ensure_smem_limit(const void* kernel, int bytes, const char* what);
 
 extern std::atomic<uint64_t> g_launches;
 
+// Peers a kernel can write to directly (one node: up to 8 GPUs, so 7 others).
+constexpr int kMaxPeers = 7;
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // Programmatic dependent launch (sm_90 and later).  A kernel started with launch_dependent()

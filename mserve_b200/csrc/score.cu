@@ -35,7 +35,22 @@ struct ScoreDev {
   int64_t total_slices;
   int64_t slices_per_warp;
   int32_t page_shift;       // log2(page_size) when it is a power of two, else -1
+  int32_t npeers;           // other ranks' copies of the score rows (mskv_score_fanout), 0..7
+  float* peers[kMaxPeers];  // each at the same offsets as `scores`, in another GPU's memory
 };
+
+// One score: this rank's row and, with fan-out, the same element of every peer's copy (a
+// plain store through the peer mapping, over NVLink).
+__device__ __forceinline__ void put_score(const ScoreDev& a, int64_t i, float v) {
+  a.scores[i] = v;
+  for (int p = 0; p < a.npeers; ++p) a.peers[p][i] = v;
+}
+
+// With fan-out, a writing thread's stores are made visible to the whole system before it
+// exits, so a flag written after this kernel (mskv_flag_signal) orders them for the peers.
+__device__ __forceinline__ void publish_scores(const ScoreDev& a) {
+  if (a.npeers) __threadfence_system();
+}
 
 template <typename T> struct Cvt;
 template <> struct Cvt<__nv_bfloat16> {
@@ -187,8 +202,9 @@ __global__ void __launch_bounds__(256) score_fast_kernel(const ScoreDev a) {
     float score = reduce_scatter<GL>(part, gl);
     if constexpr (METHOD == 1) score = sqrtf(score);
     const int64_t t = t_slice + lane;
-    if (group_ok && t < len) a.scores[seg * a.scores_stride + t] = score;
+    if (group_ok && t < len) put_score(a, seg * a.scores_stride + t, score);
   }
+  publish_scores(a);
 }
 
 // Main path for 16-bit keys: register streaming, 8 rows per lane group.
@@ -420,7 +436,7 @@ __device__ __forceinline__ void score_rows(const ScoreDev& a, const SliceRef& r,
   for (int o = 8; o < GL; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
   if constexpr (METHOD == 1) sc = sqrtf(sc);
   const int64_t t = r.t0 + (gl & 7);
-  if (gl < 8 && t < r.len) a.scores[r.seg * a.scores_stride + t] = r.ok ? sc : -INFINITY;
+  if (gl < 8 && t < r.len) put_score(a, r.seg * a.scores_stride + t, r.ok ? sc : -INFINITY);
 }
 
 template <typename T>
@@ -490,6 +506,7 @@ __global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) 
     }
     score(nxt, bufB);
   }
+  publish_scores(a);
 }
 
 template <typename T, int D, int METHOD, bool PAGED>
@@ -542,8 +559,9 @@ __global__ void __launch_bounds__(256) score_generic_kernel(const ScoreDev a) {
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) a.scores[seg * a.scores_stride + t] = METHOD == 1 ? sqrtf(acc) : acc;
+    if (lane == 0) put_score(a, seg * a.scores_stride + t, METHOD == 1 ? sqrtf(acc) : acc);
   }
+  publish_scores(a);
 }
 
 template <typename T, int D, int METHOD, bool PAGED>
@@ -605,7 +623,7 @@ static int dispatch_method(ScoreDev& a, bool paged, bool fast, bool stream16, cu
 
 using namespace mskv;
 
-extern "C" int mskv_score(const mskv_score_desc* d, void* stream) {
+static int score_impl(const mskv_score_desc* d, float* const* peers, int npeers, void* stream) {
   if (!d) return fail(MSKV_ERR_ARG, "mskv_score: NULL descriptor");
   if (d->batch < 0 || d->kv_heads <= 0 || d->q_heads <= 0 || d->head_dim <= 0 || d->max_tokens < 0)
     return fail(MSKV_ERR_ARG, "mskv_score: bad sizes");
@@ -631,6 +649,8 @@ extern "C" int mskv_score(const mskv_score_desc* d, void* stream) {
   a.scores = d->scores; a.scores_stride = d->scores_stride; a.max_tokens = d->max_tokens;
   a.batch = d->batch; a.q_heads = d->q_heads; a.kv_heads = d->kv_heads; a.head_dim = d->head_dim;
   a.method = d->method;
+  a.npeers = npeers;
+  for (int p = 0; p < npeers; ++p) a.peers[p] = peers[p];
   const bool paged = d->k.page_table != nullptr;
   a.page_shift = -1;
   if (paged && d->k.page_size > 0 && (d->k.page_size & (d->k.page_size - 1)) == 0) {
@@ -660,4 +680,14 @@ extern "C" int mskv_score(const mskv_score_desc* d, void* stream) {
     case MSKV_DT_F16: return dispatch_method<__half>(a, paged, fast, stream16, st);
     default: return dispatch_method<__nv_bfloat16>(a, paged, fast, stream16, st);
   }
+}
+
+extern "C" int mskv_score(const mskv_score_desc* d, void* stream) { return score_impl(d, nullptr, 0, stream); }
+
+extern "C" int mskv_score_fanout(const mskv_score_desc* d, float* const* peer_scores, int32_t npeers, void* stream) {
+  if (npeers < 0 || npeers > kMaxPeers) return fail(MSKV_ERR_ARG, "mskv_score_fanout: npeers must lie in [0, %d]", kMaxPeers);
+  if (npeers > 0 && !peer_scores) return fail(MSKV_ERR_ARG, "mskv_score_fanout: NULL peer_scores");
+  for (int p = 0; p < npeers; ++p)
+    if (!peer_scores[p]) return fail(MSKV_ERR_ARG, "mskv_score_fanout: NULL peer_scores[%d]", p);
+  return score_impl(d, peer_scores, npeers, stream);
 }

@@ -73,6 +73,8 @@ def check_status(device: torch.device, what: str = "kernel") -> None:
             reasons.append("page-table entry not mapped")
         if v & _lib.STATUS_DST_OOB:
             reasons.append("destination token out of range")
+        if v & _lib.STATUS_TIMEOUT:
+            reasons.append("a wait for another GPU's flag timed out")
         raise RuntimeError(f"{what}: {', '.join(reasons)} (status 0x{v:x}); offending rows were skipped")
 
 
@@ -280,11 +282,14 @@ def copy_rows(src: RowsSpec, dst: RowsSpec, *, batch: int, num_tokens: int,
 # scoring / selection
 # ---------------------------------------------------------------------------------------
 def score(q: torch.Tensor, k: RowsSpec, *, batch: int, kv_heads: int, max_tokens: int,
-          out: torch.Tensor, method: int = 0, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+          out: torch.Tensor, method: int = 0, stream: Optional[torch.cuda.Stream] = None,
+          peers: Sequence[int] = ()) -> torch.Tensor:
     """fp32 importance of every token per (b, KV head) (mskv_score).
 
     q: [B, Hq, D] (or [B, Hq, 1, D]) in the K dtype; out: fp32 [B, Hkv, >= max_tokens].
-    method 0: GQA-summed q·k; method 1: ||k||_2.
+    method 0: GQA-summed q·k; method 1: ||k||_2.  peers: device addresses of up to 7 other
+    copies of `out` (same layout, mapped from other GPUs): every score is stored there too
+    (mskv_score_fanout).
     """
     if q.dim() == 4:
         q = q[:, :, -1, :]
@@ -313,7 +318,11 @@ def score(q: torch.Tensor, k: RowsSpec, *, batch: int, kv_heads: int, max_tokens
     d.method = method
     d.batch, d.q_heads, d.kv_heads, d.head_dim = batch, Hq, kv_heads, D
     keep = (q, out, k)
-    check(lib().mskv_score(C.byref(d), _stream_ptr(stream)))
+    if peers:
+        arr = (C.c_void_p * len(peers))(*[int(p) for p in peers])
+        check(lib().mskv_score_fanout(C.byref(d), arr, len(peers), _stream_ptr(stream)))
+    else:
+        check(lib().mskv_score(C.byref(d), _stream_ptr(stream)))
     del keep
     return out
 
@@ -517,3 +526,59 @@ def image_filter(attn0: torch.Tensor, *, img_start: int, img_seq: int, text_star
     del keep
     return idx, count
 
+
+# ---------------------------------------------------------------------------------------
+# peer memory and flags (CUDA IPC; the score-row exchange between the GPUs of one node)
+# ---------------------------------------------------------------------------------------
+def ipc_alloc(nbytes: int) -> Tuple[int, bytes]:
+    """Zeroed device memory that other processes can map: (address, IPC handle bytes)."""
+    n = int(lib().mskv_ipc_handle_bytes())
+    handle = C.create_string_buffer(n)
+    ptr = C.c_void_p()
+    check(lib().mskv_ipc_alloc(int(nbytes), C.byref(ptr), handle))
+    return int(ptr.value), handle.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    """Maps another process's mskv_ipc_alloc memory into this one; returns its address here."""
+    buf = C.create_string_buffer(bytes(handle), len(handle))
+    ptr = C.c_void_p()
+    check(lib().mskv_ipc_open(buf, C.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().mskv_ipc_close(C.c_void_p(ptr)))
+
+
+def ipc_free(ptr: int) -> None:
+    check(lib().mskv_ipc_free(C.c_void_p(ptr)))
+
+
+def flag_signal(flag_arrays: Sequence[int], index: int, value: int, stream: Optional[torch.cuda.Stream] = None):
+    """Stores `value` at element `index` of every int64 flag array, after the stream's earlier work."""
+    arr = (C.c_void_p * len(flag_arrays))(*[int(p) for p in flag_arrays])
+    check(lib().mskv_flag_signal(arr, len(flag_arrays), int(index), int(value), _stream_ptr(stream)))
+
+
+def flag_wait(flags: int, count: int, value: int, *, at_least: bool = False, timeout_s: float = 1.0,
+              device: Optional[torch.device] = None, stream: Optional[torch.cuda.Stream] = None):
+    """Makes the stream wait until the `count` int64 flags at `flags` equal (or reach) `value`;
+    after timeout_s the wait gives up and sets the timeout status bit (check_status raises)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    check(lib().mskv_flag_wait(C.c_void_p(int(flags)), int(count), int(value), int(bool(at_least)),
+                               int(timeout_s * 1e9), C.c_void_p(status_word(dev).data_ptr()), _stream_ptr(stream)))
+
+
+class _DeviceArray:
+    """A device address range seen as a tensor (the CUDA array interface, no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"data": (int(ptr), False), "shape": tuple(shape), "typestr": typestr,
+                                         "version": 3, "strides": None}
+
+
+def device_tensor(ptr: int, shape, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A tensor over device memory this library allocated (the caller keeps it alive)."""
+    typestr = {torch.float32: "<f4", torch.int64: "<i8", torch.int32: "<i4"}[dtype]
+    return torch.as_tensor(_DeviceArray(ptr, shape, typestr), device=device)

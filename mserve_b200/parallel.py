@@ -16,11 +16,15 @@ Hkv / world, in its own host store, and gathers them over its own host link.
   summation order, and with it every tie, does not depend on the number of ranks.
 
 The exchange is the only collective on the path, and it moves score rows (B*T*4 bytes per
-head), never KV rows.
+head), never KV rows.  Two forms:
+* "nccl": the score kernel writes this rank's rows, then an NCCL all-gather;
+* "peer" (PeerExchange): the score kernel itself stores every row into every rank's buffer
+  through CUDA IPC mappings (mskv_score_fanout), so the rows cross NVLink while the keys are
+  still being read, and epoch flags in peer memory replace the collective.
 """
 from __future__ import annotations
 
-from typing import Optional, Tuple
+from typing import Dict, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -57,6 +61,95 @@ def exchange_head_scores(local: torch.Tensor, gathered: torch.Tensor, group=None
     return gathered
 
 
+class PeerExchange:
+    """Score rows of every rank stored straight into every rank's buffer by the score kernel.
+
+    Each rank allocates (mskv_ipc_alloc) two buffers [world, B, Hl, T] fp32 -- the call's
+    epoch e (1, 2, ...) uses parity e % 2 -- and an int64 flag array [3 * world], and maps
+    every other rank's through CUDA IPC.  One exchange (score()):
+      1. wait until every rank has finished reading this parity's buffer of epoch e - 2
+         (consumed flags, written by the readers into this rank's flags);
+      2. the score kernel stores this rank's rows into block `rank` of parity p of every
+         rank's buffer (its own directly, the others' over NVLink), and makes them
+         system-visible;
+      3. signal: ready[p][rank] = e in every rank's flags;
+      4. wait until ready[p][s] reaches e for every rank s: the buffer is complete;
+    then the caller's top-k reads it and release() writes consumed[rank] = e to every rank.
+    Every wait is bounded (timeout_s); expiry sets the timeout status bit, which
+    ops.check_status raises.  Every rank must make the same sequence of calls.
+    """
+
+    def __init__(self, batch: int, local_heads: int, max_tokens: int, *, group=None,
+                 device: Optional[torch.device] = None, timeout_s: float = 1.0):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the peer exchange spans at most 8 GPUs (one node)")
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.timeout_s = float(timeout_s)
+        self.shape = (self.world, batch, local_heads, max_tokens)
+        self.block = batch * local_heads * max_tokens            # elements of one rank's rows
+        W = self.world
+        self.buf, hb = ops.ipc_alloc(2 * W * self.block * 4)
+        self.flags, hf = ops.ipc_alloc(3 * W * 8)
+        got = [None] * W
+        dist.all_gather_object(got, (hb, hf, self.shape), group=group)
+        self.peer_buf: Dict[int, int] = {}
+        self.peer_flags: Dict[int, int] = {}
+        for r, (hbr, hfr, shape) in enumerate(got):
+            if tuple(shape) != self.shape:
+                raise ValueError(f"rank {r} exchanges {tuple(shape)}, this rank {self.shape}")
+            if r == self.rank:
+                self.peer_buf[r], self.peer_flags[r] = self.buf, self.flags
+            else:
+                self.peer_buf[r], self.peer_flags[r] = ops.ipc_open(hbr), ops.ipc_open(hfr)
+        self.views = [ops.device_tensor(self.buf + p * W * self.block * 4, self.shape, torch.float32, self.device)
+                      for p in (0, 1)]
+        self.epoch = 0
+        self.closed = False
+
+    def _rows_at(self, r: int, parity: int) -> int:
+        """Address of this rank's block in parity `parity` of rank r's buffer."""
+        return self.peer_buf[r] + ((parity * self.world + self.rank) * self.block) * 4
+
+    def score(self, q_local: torch.Tensor, k_local: ops.RowsSpec, *, max_tokens: int, method: int = 0) -> torch.Tensor:
+        """Scores this rank's heads into every rank's buffer; returns this rank's complete
+        [world, B, Hl, T] buffer of the new epoch (valid until release() of the epoch after)."""
+        W, e = self.world, self.epoch + 1
+        p = e % 2
+        flags = [self.peer_flags[r] for r in range(W)]
+        if e > 2:
+            ops.flag_wait(self.flags + 2 * W * 8, W, e - 2, at_least=True, timeout_s=self.timeout_s,
+                          device=self.device)
+        _, B, Hl, T = self.shape
+        ops.score(q_local, k_local, batch=B, kv_heads=Hl, max_tokens=max_tokens, out=self.views[p][self.rank],
+                  method=method, peers=[self._rows_at(r, p) for r in range(W) if r != self.rank])
+        ops.flag_signal(flags, p * W + self.rank, e)
+        ops.flag_wait(self.flags + p * W * 8, W, e, at_least=True, timeout_s=self.timeout_s, device=self.device)
+        self.epoch = e
+        return self.views[p]
+
+    def release(self) -> None:
+        """The caller has finished reading the last score() buffer (stream order)."""
+        ops.flag_signal([self.peer_flags[r] for r in range(self.world)], 2 * self.world + self.rank, self.epoch)
+
+    def close(self) -> None:
+        """Unmaps the peers' memory and frees this rank's (collective: every rank calls it)."""
+        if self.closed:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)           # nobody reads or writes the buffers any more
+        for r in range(self.world):
+            if r != self.rank:
+                ops.ipc_close(self.peer_buf[r])
+                ops.ipc_close(self.peer_flags[r])
+        dist.barrier(group=self.group)           # every mapping of this rank's memory is closed
+        ops.ipc_free(self.buf)
+        ops.ipc_free(self.flags)
+        self.closed = True
+
+
 class SharedSelection:
     """Shared (per-sequence) selection over KV heads sharded across the ranks of `group`.
 
@@ -66,7 +159,7 @@ class SharedSelection:
     """
 
     def __init__(self, batch: int, kv_heads: int, q_heads: int, max_tokens: int, *, group=None,
-                 device: Optional[torch.device] = None):
+                 device: Optional[torch.device] = None, exchange: str = "nccl", timeout_s: float = 1.0):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -77,9 +170,17 @@ class SharedSelection:
         self.Hl = self.h1 - self.h0
         self.G = q_heads // kv_heads
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self.local = torch.empty(batch, self.Hl, max_tokens, dtype=torch.float32, device=self.device)
-        self.gathered = torch.empty(self.world, batch, self.Hl, max_tokens, dtype=torch.float32,
-                                    device=self.device)
+        if exchange not in ("nccl", "peer"):
+            raise ValueError("exchange must be 'nccl' or 'peer'")
+        self.exchange = exchange
+        self.peer = None
+        if exchange == "peer":
+            self.peer = PeerExchange(batch, self.Hl, max_tokens, group=group, device=self.device,
+                                     timeout_s=timeout_s)
+        else:
+            self.local = torch.empty(batch, self.Hl, max_tokens, dtype=torch.float32, device=self.device)
+            self.gathered = torch.empty(self.world, batch, self.Hl, max_tokens, dtype=torch.float32,
+                                        device=self.device)
 
     def q_heads_local(self) -> Tuple[int, int]:
         """The query heads [q0, q1) whose KV heads this rank holds."""
@@ -96,10 +197,21 @@ class SharedSelection:
         counts int32 [B]).
         """
         T = self.T if len_scalar is None else int(len_scalar)
-        ops.score(q_local, k_local, batch=self.B, kv_heads=self.Hl, max_tokens=T, out=self.local,
-                  method=method)
-        exchange_head_scores(self.local, self.gathered, self.group)
+        if self.peer is not None:
+            gathered = self.peer.score(q_local, k_local, max_tokens=T, method=method)
+        else:
+            ops.score(q_local, k_local, batch=self.B, kv_heads=self.Hl, max_tokens=T, out=self.local,
+                      method=method)
+            gathered = exchange_head_scores(self.local, self.gathered, self.group)
         scale = 1.0 / self.Hq if method == 0 else 1.0 / self.Hkv
-        return ops.topk(self.gathered, top_k=top_k, recent=recent, len_=len_, len_scalar=T,
-                        rows_per_sel=self.Hkv, sel_per_batch=1, scale=scale, out=out, counts=counts,
-                        out_dtype=out_dtype, row_blocks=(self.world, self.B, self.Hl))
+        res = ops.topk(gathered, top_k=top_k, recent=recent, len_=len_, len_scalar=T,
+                       rows_per_sel=self.Hkv, sel_per_batch=1, scale=scale, out=out, counts=counts,
+                       out_dtype=out_dtype, row_blocks=(self.world, self.B, self.Hl))
+        if self.peer is not None:
+            self.peer.release()
+        return res
+
+    def close(self) -> None:
+        """Releases the peer exchange's memory (collective with exchange='peer')."""
+        if self.peer is not None:
+            self.peer.close()
