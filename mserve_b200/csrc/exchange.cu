@@ -42,7 +42,12 @@ struct SignalArgs {
   int64_t value;
 };
 
+// Both flag kernels are launched programmatically dependent on the kernel before them (so
+// their launch overlaps its tail) and begin with the hardware grid-dependency wait: they touch
+// no flag before that kernel has completed, so a wait never spins beside another kernel of
+// this GPU that it depends on.
 __global__ void flag_signal_kernel(const SignalArgs a) {
+  wait_for_previous_grid();
   __threadfence_system();
   const int r = threadIdx.x;
   if (r < a.nranks) store_release_sys(a.flags[r] + a.index, a.value);
@@ -50,6 +55,7 @@ __global__ void flag_signal_kernel(const SignalArgs a) {
 
 __global__ void flag_wait_kernel(const int64_t* flags, int count, int64_t value, int at_least, uint64_t timeout_ns,
                                  uint32_t* status) {
+  wait_for_previous_grid();
   const int i = threadIdx.x;
   if (i < count) {
     const uint64_t t0 = global_ns();
@@ -64,6 +70,7 @@ __global__ void flag_wait_kernel(const int64_t* flags, int count, int64_t value,
     }
   }
   __threadfence();
+  allow_dependents();
 }
 
 }  // namespace mskv
@@ -117,7 +124,8 @@ extern "C" int mskv_flag_signal(int64_t* const* flags, int32_t nranks, int32_t i
   a.nranks = nranks;
   a.index = index;
   a.value = value;
-  flag_signal_kernel<<<1, 32, 0, as_stream(stream)>>>(a);
+  const cudaError_t e = launch_dependent(flag_signal_kernel, dim3(1), dim3(32), 0, as_stream(stream), a);
+  if (e != cudaSuccess) return cuda_status(e, "mskv_flag_signal launch");
   return after_launch("mskv_flag_signal");
 }
 
@@ -128,6 +136,8 @@ extern "C" int mskv_flag_wait(const int64_t* flags, int32_t count, int64_t value
   if (timeout_ns == 0 || timeout_ns > 60ull * 1000000000ull)
     return fail(MSKV_ERR_ARG, "mskv_flag_wait: timeout must lie in (0, 60 s]");
   const int threads = (count + 31) / 32 * 32;
-  flag_wait_kernel<<<1, threads, 0, as_stream(stream)>>>(flags, count, value, at_least, timeout_ns, status);
+  const cudaError_t e = launch_dependent(flag_wait_kernel, dim3(1), dim3(threads), 0, as_stream(stream), flags,
+                                         count, value, at_least, timeout_ns, status);
+  if (e != cudaSuccess) return cuda_status(e, "mskv_flag_wait launch");
   return after_launch("mskv_flag_wait");
 }
