@@ -76,8 +76,6 @@ def main():
             ev[2].record()
             ops.topk(gathered, top_k=K, recent=R, len_scalar=T, rows_per_sel=Hkv, sel_per_batch=1,
                      scale=scale, out=idx, counts=cnt, row_blocks=(world, B, sel.Hl))
-            if sel.peer is not None:
-                sel.peer.release()
             ev[3].record()
             return ev
 

@@ -65,22 +65,24 @@ class PeerExchange:
     """Score rows of every rank stored straight into every rank's buffer by the score kernel.
 
     Each rank allocates (mskv_ipc_alloc) two buffers [world, B, Hl, T] fp32 -- the call's
-    epoch e (1, 2, ...) uses parity e % 2 -- and an int64 flag array [3 * world], and maps
+    epoch e (1, 2, ...) uses parity e % 2 -- and an int64 flag array ready[2][world], and maps
     every other rank's through CUDA IPC.  One exchange (score()):
-      1. wait until every rank has finished reading this parity's buffer of epoch e - 2
-         (consumed flags, written by the readers into this rank's flags);
-      2. the score kernel stores this rank's rows into block `rank` of parity p of every
-         rank's buffer (its own directly, the others' over NVLink), and makes them
+      1. the score kernel stores this rank's rows into block `rank` of parity p of every
+         rank's buffer (its own directly, the others' over NVLink) and makes them
          system-visible;
-      3. signal: ready[p][rank] = e in every rank's flags;
-      4. wait until ready[p][s] reaches e for every rank s: the buffer is complete;
-    then the caller's top-k reads it and release() writes consumed[rank] = e to every rank.
-    Every wait is bounded (timeout_s); expiry sets the timeout status bit, which
-    ops.check_status raises.  Every rank must make the same sequence of calls.
+      2. signal: ready[p][rank] = e in every rank's flags;
+      3. wait until ready[p][s] reaches e for every rank s: the buffer is complete.
+    The caller then reads the buffer (the top-k) on the same stream.  Two buffers make a
+    separate "consumed" handshake unnecessary: a rank writes parity p again at epoch e + 2
+    only after every rank signalled epoch e + 1, which each does after its stream finished
+    reading epoch e.  Every wait is bounded (timeout_s); expiry sets the timeout status bit,
+    which ops.check_status raises.  Every rank must make the same sequence of calls.
     """
 
     def __init__(self, batch: int, local_heads: int, max_tokens: int, *, group=None,
-                 device: Optional[torch.device] = None, timeout_s: float = 1.0):
+                 device: Optional[torch.device] = None, timeout_s: float = 1.0, backend=None):
+        # backend: the memory, flag and score operations (default: the CUDA library, ops)
+        self.ops = backend if backend is not None else ops
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -91,8 +93,8 @@ class PeerExchange:
         self.shape = (self.world, batch, local_heads, max_tokens)
         self.block = batch * local_heads * max_tokens            # elements of one rank's rows
         W = self.world
-        self.buf, hb = ops.ipc_alloc(2 * W * self.block * 4)
-        self.flags, hf = ops.ipc_alloc(3 * W * 8)
+        self.buf, hb = self.ops.ipc_alloc(2 * W * self.block * 4)
+        self.flags, hf = self.ops.ipc_alloc(2 * W * 8)
         got = [None] * W
         dist.all_gather_object(got, (hb, hf, self.shape), group=group)
         self.peer_buf: Dict[int, int] = {}
@@ -103,8 +105,8 @@ class PeerExchange:
             if r == self.rank:
                 self.peer_buf[r], self.peer_flags[r] = self.buf, self.flags
             else:
-                self.peer_buf[r], self.peer_flags[r] = ops.ipc_open(hbr), ops.ipc_open(hfr)
-        self.views = [ops.device_tensor(self.buf + p * W * self.block * 4, self.shape, torch.float32, self.device)
+                self.peer_buf[r], self.peer_flags[r] = self.ops.ipc_open(hbr), self.ops.ipc_open(hfr)
+        self.views = [self.ops.device_tensor(self.buf + p * W * self.block * 4, self.shape, torch.float32, self.device)
                       for p in (0, 1)]
         self.epoch = 0
         self.closed = False
@@ -115,38 +117,32 @@ class PeerExchange:
 
     def score(self, q_local: torch.Tensor, k_local: ops.RowsSpec, *, max_tokens: int, method: int = 0) -> torch.Tensor:
         """Scores this rank's heads into every rank's buffer; returns this rank's complete
-        [world, B, Hl, T] buffer of the new epoch (valid until release() of the epoch after)."""
+        [world, B, Hl, T] buffer of the new epoch, to be read on the current stream before the
+        next call's score kernel (which follows on the same stream)."""
         W, e = self.world, self.epoch + 1
         p = e % 2
-        flags = [self.peer_flags[r] for r in range(W)]
-        if e > 2:
-            ops.flag_wait(self.flags + 2 * W * 8, W, e - 2, at_least=True, timeout_s=self.timeout_s,
-                          device=self.device)
         _, B, Hl, T = self.shape
-        ops.score(q_local, k_local, batch=B, kv_heads=Hl, max_tokens=max_tokens, out=self.views[p][self.rank],
-                  method=method, peers=[self._rows_at(r, p) for r in range(W) if r != self.rank])
-        ops.flag_signal(flags, p * W + self.rank, e)
-        ops.flag_wait(self.flags + p * W * 8, W, e, at_least=True, timeout_s=self.timeout_s, device=self.device)
+        self.ops.score(q_local, k_local, batch=B, kv_heads=Hl, max_tokens=max_tokens, out=self.views[p][self.rank],
+                       method=method, peers=[self._rows_at(r, p) for r in range(W) if r != self.rank])
+        self.ops.flag_signal([self.peer_flags[r] for r in range(W)], p * W + self.rank, e)
+        self.ops.flag_wait(self.flags + p * W * 8, W, e, at_least=True, timeout_s=self.timeout_s, device=self.device)
         self.epoch = e
         return self.views[p]
-
-    def release(self) -> None:
-        """The caller has finished reading the last score() buffer (stream order)."""
-        ops.flag_signal([self.peer_flags[r] for r in range(self.world)], 2 * self.world + self.rank, self.epoch)
 
     def close(self) -> None:
         """Unmaps the peers' memory and frees this rank's (collective: every rank calls it)."""
         if self.closed:
             return
-        torch.cuda.synchronize(self.device)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)           # nobody reads or writes the buffers any more
         for r in range(self.world):
             if r != self.rank:
-                ops.ipc_close(self.peer_buf[r])
-                ops.ipc_close(self.peer_flags[r])
+                self.ops.ipc_close(self.peer_buf[r])
+                self.ops.ipc_close(self.peer_flags[r])
         dist.barrier(group=self.group)           # every mapping of this rank's memory is closed
-        ops.ipc_free(self.buf)
-        ops.ipc_free(self.flags)
+        self.ops.ipc_free(self.buf)
+        self.ops.ipc_free(self.flags)
         self.closed = True
 
 
@@ -207,8 +203,6 @@ class SharedSelection:
         res = ops.topk(gathered, top_k=top_k, recent=recent, len_=len_, len_scalar=T,
                        rows_per_sel=self.Hkv, sel_per_batch=1, scale=scale, out=out, counts=counts,
                        out_dtype=out_dtype, row_blocks=(self.world, self.B, self.Hl))
-        if self.peer is not None:
-            self.peer.release()
         return res
 
     def close(self) -> None:

@@ -103,3 +103,113 @@ def test_blocked_layout_single_block_is_plain_rows():
     for j in range(5):
         for r in range(4):
             assert j * sel_stride + (r // row_block) * block_stride + (r % row_block) * 100 == (j * 4 + r) * 100
+
+
+class _SharedMemoryBackend:
+    """The peer exchange's memory, flag and score operations on the CPU, for its host logic:
+    shared-memory segments stand in for IPC device memory (an "address" is a registered base
+    plus an offset), flag waits poll the segment from the host, and the score is the oracle's
+    GQA-summed rows.  Every store into a peer goes through the same address arithmetic that
+    the CUDA path hands to the kernels."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.segs = {}                  # base -> (SharedMemory, size)
+        self.next = (rank + 1) << 40
+
+    def _register(self, shm, size):
+        base = self.next
+        self.next += 1 << 32
+        self.segs[base] = (shm, size)
+        return base
+
+    def _view(self, addr, count, dtype):
+        for base, (shm, size) in self.segs.items():
+            if base <= addr < base + size:
+                off = addr - base
+                assert off + count * np.dtype(dtype).itemsize <= size, "access beyond the allocation"
+                return np.ndarray((count,), dtype=dtype, buffer=shm.buf, offset=off)
+        raise AssertionError(f"address {addr:#x} is in no allocation")
+
+    def ipc_alloc(self, nbytes):
+        from multiprocessing import shared_memory
+        shm = shared_memory.SharedMemory(create=True, size=nbytes)
+        np.ndarray((nbytes,), dtype=np.uint8, buffer=shm.buf)[:] = 0
+        return self._register(shm, nbytes), shm.name.encode()
+
+    def ipc_open(self, handle):
+        from multiprocessing import shared_memory
+        shm = shared_memory.SharedMemory(name=handle.decode())
+        return self._register(shm, shm.size)
+
+    def ipc_close(self, ptr):
+        shm, _ = self.segs.pop(ptr)
+        shm.close()
+
+    def ipc_free(self, ptr):
+        shm, _ = self.segs.pop(ptr)
+        shm.close()
+        shm.unlink()
+
+    def device_tensor(self, ptr, shape, dtype, device):
+        n = int(np.prod(shape))
+        return torch.from_numpy(self._view(ptr, n, np.float32).reshape(shape))
+
+    def score(self, q, k, *, batch, kv_heads, max_tokens, out, method=0, peers=()):
+        rows = ko.gqa_scores(q, k).astype(np.float32)[:, :, :max_tokens]
+        out[:, :, :max_tokens] = torch.from_numpy(rows)
+        n = batch * kv_heads * out.shape[2]
+        for p in peers:
+            self._view(p, n, np.float32).reshape(out.shape)[:, :, :max_tokens] = rows
+
+    def flag_signal(self, flag_arrays, index, value, stream=None):
+        for f in flag_arrays:
+            self._view(f + index * 8, 1, np.int64)[0] = value
+
+    def flag_wait(self, flags, count, value, *, at_least=False, timeout_s=1.0, device=None, stream=None):
+        import time
+        v = self._view(flags, count, np.int64)
+        t0 = time.monotonic()
+        while not all((x >= value) if at_least else (x == value) for x in v):
+            if time.monotonic() - t0 > timeout_s:
+                raise TimeoutError(f"flags {list(v)} did not reach {value}")
+            time.sleep(0.0005)
+
+
+def _peer_worker(rank, world, port, epochs):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from mserve_b200 import parallel
+        B, Hq, Hkv, T, D = 2, 16, 8, 100, 16
+        Hl = Hkv // world
+        G = Hq // Hkv
+        be = _SharedMemoryBackend(rank)
+        ex = parallel.PeerExchange(B, Hl, T, device=torch.device("cpu"), timeout_s=20.0, backend=be)
+        rng = np.random.default_rng(rank)
+        for e in range(1, epochs + 1):
+            q, k = _case(100 + e, B=B, Hq=Hq, Hkv=Hkv, T=T, D=D)       # the same on every rank
+            h0, h1 = rank * Hl, (rank + 1) * Hl
+            if rng.random() < 0.5:                                    # ranks drift apart
+                import time
+                time.sleep(rng.random() * 0.02)
+            view = ex.score(q[:, h0 * G:h1 * G], k[:, h0:h1], max_tokens=T)
+            if rng.random() < 0.5:                                    # a slow reader of the buffer
+                import time
+                time.sleep(rng.random() * 0.02)
+            got = view.numpy().copy()
+            want = ko.gqa_scores(q, k).astype(np.float32).reshape(B, world, Hl, T).transpose(1, 0, 2, 3)
+            np.testing.assert_array_equal(got, want, err_msg=f"rank {rank} epoch {e}")
+            assert ex.epoch == e
+        ex.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_exchange_protocol(world):
+    """PeerExchange's buffer parities, block offsets and epoch flags on gloo ranks: every
+    epoch's gathered buffer holds every rank's rows of that epoch (none of another epoch),
+    while ranks drift apart and read their buffers late by random delays."""
+    mp.start_processes(_peer_worker, args=(world, _free_port(), 7), nprocs=world, join=True, start_method="spawn")

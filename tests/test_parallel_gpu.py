@@ -176,7 +176,7 @@ def _single_rank(fn):
 
 def test_peer_exchange_one_rank_epochs(built_lib):
     """SharedSelection with the peer exchange on one rank: five successive selections (both
-    buffer parities, the consumed-flag waits from the third on) equal the NCCL form's."""
+    buffer parities) equal the NCCL form's."""
     from mserve_b200 import ops, parallel
 
     def body(dev):
