@@ -9,7 +9,8 @@ Workloads: Qwen2.5-VL-7B's 28 heads, 15 system tokens, an image of 1296 tokens (
 logits.
 
 Arms, each on the same map and checked to keep the same tokens:
-  * mserve: selection.dual_attention_filter (two kernels plus the read of the kept count);
+  * mserve: selection.dual_attention_filter (a counter reset and one kernel, then the read of
+    the kept count);
   * reference: the reference function's torch operations on the GPU, as it runs them (head
     mean, column sum and max, the two thresholds, the boolean index).
 Per arm: the call's wall time up to the kept indices being usable on the host side (a device
