@@ -80,7 +80,7 @@ class PeerExchange:
     """
 
     def __init__(self, batch: int, local_heads: int, max_tokens: int, *, group=None,
-                 device: Optional[torch.device] = None, timeout_s: float = 1.0, backend=None):
+                 device: Optional[torch.device] = None, timeout_s: float = 5.0, backend=None):
         # backend: the memory, flag and score operations (default: the CUDA library, ops)
         self.ops = backend if backend is not None else ops
         self.group = group
@@ -155,7 +155,7 @@ class SharedSelection:
     """
 
     def __init__(self, batch: int, kv_heads: int, q_heads: int, max_tokens: int, *, group=None,
-                 device: Optional[torch.device] = None, exchange: str = "nccl", timeout_s: float = 1.0):
+                 device: Optional[torch.device] = None, exchange: str = "nccl", timeout_s: float = 5.0):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
