@@ -46,3 +46,29 @@ def test_workload_lengths_and_gathered_bytes():
     eng.top_k_ratio, eng.topk_h = 0.1, np.array([10, 1, 0])
     rows = (10 + 8) + (0 + 5) + 0
     assert bench.gathered_bytes(eng) == 2 * rows * 2 * 4 * 2
+
+
+def test_reference_arm_json_line():
+    """bench.py --impl reference on this machine's cores: one JSON line with the bench
+    contract's keys, the same metric as the product arm, a cpu_baseline describing the run and
+    an e2e object with no host<->device bytes."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    import bench
+    root = Path(bench.__file__).resolve().parent
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0"],
+                       cwd=root, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC
+    assert line["unit"] == "GB/s" and line["higher_is_better"] is True and line["value"] > 0
+    assert line["n_gpus"] == 1 and line["steps"] == 1 and line["warmup"] == 0
+    assert line["config"]["workload"] == bench.WORKLOADS["qwen7b"][1]
+    cb = line["cpu_baseline"]
+    assert cb["value"] == line["value"] and cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
