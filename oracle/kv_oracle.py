@@ -367,26 +367,21 @@ def _stage(x, stage: str) -> np.ndarray:
     return x
 
 
-def dual_attention_filter(attn: np.ndarray, v_token_start: int, img_seq: int, global_thr: float = 1.0,
-                          individual_thr: float = 0.0, stage: str = "f32"):
-    """Restates dual_attention_filter (qwen-eljrte/Qwen_Transformer/dual_attention_filter.py:6-103).
-
-    attn [B, H, T, T] (batch 0 used).  block = attn[0, :, text rows, image columns] (lines
-    37-43), rounded to the stage dtype (its .half() when use_fp16, line 47); head_mean = mean
-    over heads (line 50); attn_sum = column sums over the text rows (line 54); text_max =
-    column maxima (line 57); an image token is dropped when attn_sum < attn_sum.sum() *
-    global_thr and text_max < individual_thr (line 62).  As torch tensors of the block's dtype,
-    every stage result is rounded to `stage` ('f32', 'f16' or 'bf16'), the sums accumulating in
-    float32.  The summation order is fixed: heads in order; text rows in blocks of 32, each
-    summed in order and the block sums added in order; the total over tiles of 32 columns the
-    same way.  Returns (kept image-token indices ascending, text_seq,
-    attn_sum, text_max, threshold total * global_thr as a float).
+def image_filter_block(block: np.ndarray, global_thr: float, individual_thr: float, stage: str = "f32"):
+    """The decision part of dual_attention_filter (qwen-eljrte/Qwen_Transformer/
+    dual_attention_filter.py:47-70) on the text x image block [H, text, img] itself: rounded to
+    the stage dtype (its .half() when use_fp16, line 47); head_mean = mean over heads (line 50);
+    attn_sum = column sums over the text rows (line 54); text_max = column maxima (line 57); an
+    image token is dropped when attn_sum < attn_sum.sum() * global_thr and text_max <
+    individual_thr (line 62).  As torch tensors of the block's dtype, every stage result is
+    rounded to `stage` ('f32', 'f16' or 'bf16'), the sums accumulating in float32.  The
+    summation order is fixed: heads in order; text rows in blocks of 32, each summed in order
+    and the block sums added in order; the total over tiles of 32 columns the same way.
+    Returns (kept image-token indices ascending, attn_sum, text_max, threshold total *
+    global_thr as a float).
     """
-    B, H, T, _ = attn.shape
-    text_seq = T - img_seq - v_token_start
-    img_beg, img_end = v_token_start, v_token_start + img_seq
-    txt_beg, txt_end = img_end, img_end + text_seq
-    block = _stage(np.asarray(attn[0, :, txt_beg:txt_end, img_beg:img_end], dtype=np.float32), stage)
+    H, text_seq, img_seq = block.shape
+    block = _stage(np.asarray(block, dtype=np.float32), stage)
     hs = np.zeros(block.shape[1:], dtype=np.float32)
     for h in range(H):
         hs = (hs + block[h]).astype(np.float32)
@@ -408,4 +403,21 @@ def dual_attention_filter(attn: np.ndarray, v_token_start: int, img_seq: int, gl
     total = _stage(np.float32(t), stage)
     thr = _stage(total * np.float32(global_thr), stage)[()]
     drop = (attn_sum < thr) & (text_max < np.float32(individual_thr))
-    return np.nonzero(~drop)[0].astype(np.int64), int(text_seq), attn_sum, text_max, float(thr)
+    return np.nonzero(~drop)[0].astype(np.int64), attn_sum, text_max, float(thr)
+
+
+def dual_attention_filter(attn: np.ndarray, v_token_start: int, img_seq: int, global_thr: float = 1.0,
+                          individual_thr: float = 0.0, stage: str = "f32"):
+    """Restates dual_attention_filter (qwen-eljrte/Qwen_Transformer/dual_attention_filter.py:6-103).
+
+    attn [B, H, T, T] (batch 0 used).  block = attn[0, :, text rows, image columns] (lines
+    37-43), then image_filter_block.  Returns (kept image-token indices ascending, text_seq,
+    attn_sum, text_max, threshold total * global_thr as a float).
+    """
+    B, H, T, _ = attn.shape
+    text_seq = T - img_seq - v_token_start
+    img_beg, img_end = v_token_start, v_token_start + img_seq
+    txt_beg, txt_end = img_end, img_end + text_seq
+    block = np.asarray(attn[0, :, txt_beg:txt_end, img_beg:img_end], dtype=np.float32)
+    kept, attn_sum, text_max, thr = image_filter_block(block, global_thr, individual_thr, stage)
+    return kept, int(text_seq), attn_sum, text_max, thr
