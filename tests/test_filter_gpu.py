@@ -85,3 +85,35 @@ def test_filter_strided_view_and_edges(built_lib):
     with pytest.raises(ValueError):
         ops.image_filter(attn[0].cuda().half(), img_start=0, img_seq=4, text_start=4, text_seq=2, global_thr=1.0,
                          individual_thr=0.0, round_f16=True)
+
+
+@pytest.mark.parametrize("H,text,img,dtype", [
+    (40, 33, 2500, torch.float32),     # 40 heads: two full head batches and a remainder; 3 rounds
+    (3, 1, 3000, torch.bfloat16),      # one text row: 32-thread CTAs, 94 compaction rounds
+    (2, 2, 70000, torch.float32),      # more tiles than the last CTA keeps in shared memory
+])
+def test_filter_block_edges(built_lib, H, text, img, dtype):
+    """mskv_image_filter on a [H, text, img] block at the edges of its launch shapes, against
+    the oracle's block form (same stage rounding and summation order): identical kept sets."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(H * 1000 + text)
+    # a third of the columns at twice the scale (kept by their sum); a tenth at a small scale
+    # with one large element (kept, where the text has several rows, by their maximum alone)
+    order = torch.randperm(img, generator=g)
+    scale = torch.ones(img)
+    scale[order[:img // 3]] = 2.0
+    spikes = order[img // 3:img // 3 + img // 10]
+    scale[spikes] = 0.3
+    block = torch.rand(H, text, img, generator=g) * scale
+    block[torch.randint(H, (spikes.numel(),), generator=g), torch.randint(text, (spikes.numel(),), generator=g),
+          spikes] += (1 + torch.rand(spikes.numel(), generator=g)) * 2 * H
+    block = block.to(dtype)
+    stage = "bf16" if dtype == torch.bfloat16 else "f32"
+    _, _, text_max, _ = ko.image_filter_block(block.float().numpy(), 0.0, 0.0, stage)
+    gthr, ithr = 1.0 / img, float(np.quantile(text_max, 0.9))   # the mean share; the top tenth's maxima
+    kept, attn_sum, _, thr = ko.image_filter_block(block.float().numpy(), gthr, ithr, stage)
+    assert 0 < kept.size < img
+    idx, count = ops.image_filter(block.cuda(), img_start=0, img_seq=img, text_start=0, text_seq=text,
+                                  global_thr=gthr, individual_thr=ithr)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(idx[:int(count.item())].cpu().numpy(), kept)
