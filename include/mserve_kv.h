@@ -322,9 +322,11 @@ int mskv_sparse_attention_noalloc(const mskv_attn_desc* d, void* stream);
  *   sum_j   = stage(sum_i hm[i,j]),  max_j = max_i hm[i,j],  total = stage(sum_j sum_j)
  * (text rows in blocks of 32, each summed in order, block sums in order; the total over tiles
  * of 32 columns the same way).  Image token j is dropped when sum_j < stage(total*global_thr)
- * and max_j < individual_thr; the kept ones are written to out_idx (int64, ascending; img_seq
- * entries of room) and their number to *out_count (device int32).  workspace: mskv_image_filter_workspace_bytes(img_seq, text_seq) bytes of device
- * memory (row-block partials, column sums and maxima, tile totals), 4-byte aligned. */
+ * and max_j < stage(individual_thr) (the threshold rounded to the stage dtype, as torch casts a
+ * Python scalar to the tensor's dtype before comparing); the kept ones are written to out_idx
+ * (int64, ascending; img_seq entries of room) and their number to *out_count (device int32).
+ * workspace: mskv_image_filter_workspace_bytes(img_seq, text_seq) bytes of device memory
+ * (row-block partials, column sums and maxima, tile totals), 4-byte aligned. */
 typedef struct mskv_filter_desc {
   const void* attn;
   int64_t stride_h;

@@ -11,7 +11,10 @@
 // (fp16 after its optional .half()): the head mean, the column sums and maxima, the total and
 // total * global_thr are each rounded to that dtype, with fp32 accumulation inside each
 // reduction.  The kernels do the same: fp32 sums, the stage results rounded to the stage
-// dtype (fp32, fp16 or bf16); individual_thr is compared as an fp32 scalar.
+// dtype (fp32, fp16 or bf16).  individual_thr is rounded to the stage dtype too: torch casts a
+// Python scalar to the tensor's dtype before `text_max < individual_thr`, so for a 16-bit block
+// a threshold that rounds down (bf16(0.001) = 0.00099945...) keeps a column whose maximum
+// equals the rounded value.
 //
 // Summation order, fixed (so the result does not depend on the launch shape):
 //   head mean   hm[i,j] = stage((sum over heads in order) / H)
@@ -141,17 +144,18 @@ __device__ void filter_finish(const FilterDev& a) {
   }
   __syncthreads();
   const float thr = s_thr;
+  const float ithr = stage<S>(a.individual_thr);
   uint32_t base = 0;
 #pragma unroll
   for (int r = 0; r < kPrefetchRounds; ++r) {
     if (r * nt >= a.img) break;
     const int j = r * nt + tid;
-    const bool keep = j < a.img && !(pcs[r] < thr && pcm[r] < a.individual_thr);
+    const bool keep = j < a.img && !(pcs[r] < thr && pcm[r] < ithr);
     compact_round(a, j, keep, base, s_wcnt, s_wpre, &s_round);
   }
   for (int j0 = kPrefetchRounds * nt; j0 < a.img; j0 += nt) {
     const int j = j0 + tid;
-    const bool keep = j < a.img && !(__ldcg(a.col_sum + j) < thr && __ldcg(a.col_max + j) < a.individual_thr);
+    const bool keep = j < a.img && !(__ldcg(a.col_sum + j) < thr && __ldcg(a.col_max + j) < ithr);
     compact_round(a, j, keep, base, s_wcnt, s_wpre, &s_round);
   }
   if (tid == 0) *a.out_count = (int32_t)base;

@@ -143,7 +143,8 @@ def dual_attention_filter(attn: torch.Tensor, v_token_start: int, img_seq: int, 
     text_seq = T - img_seq - v_token_start).  min_keep_ratio is accepted and, as in the
     reference, not applied.  Each stage (head mean, column sums, total, threshold) is rounded to
     the block's dtype, fp16 when use_fp16 rounds an fp32 block first, as the reference's tensor
-    arithmetic does; the sums accumulate in fp32.
+    arithmetic does; the sums accumulate in fp32.  individual_thr is rounded to that dtype too
+    before the comparison, as torch casts a Python scalar to a tensor's dtype.
     """
     if attn.dim() != 4:
         raise AssertionError("attn must be [B, H, T, T]")

@@ -402,7 +402,10 @@ def image_filter_block(block: np.ndarray, global_thr: float, individual_thr: flo
         t = np.float32(t + ts)
     total = _stage(np.float32(t), stage)
     thr = _stage(total * np.float32(global_thr), stage)[()]
-    drop = (attn_sum < thr) & (text_max < np.float32(individual_thr))
+    # torch compares a 16-bit tensor with a Python scalar after casting the scalar to the
+    # tensor's dtype (line 62), so the individual threshold is rounded to the stage dtype too
+    ithr = _stage(np.float32(individual_thr), stage)[()]
+    drop = (attn_sum < thr) & (text_max < ithr)
     return np.nonzero(~drop)[0].astype(np.int64), attn_sum, text_max, float(thr)
 
 

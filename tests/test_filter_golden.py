@@ -16,19 +16,24 @@ import torch
 from oracle import kv_oracle as ko
 
 FIX = Path(__file__).resolve().parent / "golden" / "filter_vectors.npz"
-CASES = ["thr_small", "heads28", "defaults", "bf16", "fp16_round", "callsite"]
+CASES = ["thr_small", "heads28", "defaults", "bf16", "fp16_round", "callsite", "ithr_bf16", "ithr_f16",
+         "ithr_fp16_mode"]
+# cases whose columns 10, 50 and 120 hold, in one text row, the individual threshold rounded to
+# the stage dtype, the value below it and the value above it (tests/golden/make_filter_golden.py)
+ITHR_CASES = ["ithr_bf16", "ithr_f16", "ithr_fp16_mode"]
+ITHR_COLUMNS = (10, 50, 120)
 # one unit in the last place, relative: fp32 order effects / fp16 / bf16
 STAGE_RTOL = {"f32": 1e-6, "f16": 2.0 ** -10, "bf16": 2.0 ** -7}
 
 
 def load_case(fix, name):
-    H, start, img, text, T, fp16, bf16 = (int(x) for x in fix[f"{name}/meta"])
+    H, start, img, text, T, fp16, bf16, f16 = (int(x) for x in fix[f"{name}/meta"])
     gthr, ithr = (float(x) for x in fix[f"{name}/thr"])
     blk = fix[f"{name}/block"]
     block = torch.from_numpy(blk.view(np.int16)).view(torch.bfloat16) if bf16 else torch.from_numpy(blk)
     attn = torch.zeros(1, H, T, T, dtype=block.dtype)
     attn[0, :, start + img:start + img + text, start:start + img] = block
-    stage = "f16" if fp16 else ("bf16" if bf16 else "f32")
+    stage = "f16" if (fp16 or f16) else ("bf16" if bf16 else "f32")
     return attn, dict(H=H, start=start, img=img, text=text, gthr=gthr, ithr=ithr, fp16=bool(fp16), bf16=bool(bf16),
                       stage=stage)
 
@@ -65,6 +70,19 @@ def test_filter_oracle_matches_reference(fix, name):
     np.testing.assert_allclose(text_max, fix[f"{name}/text_max"], rtol=rtol, atol=0)
     np.testing.assert_allclose(attn_sum, fix[f"{name}/attn_sum"], rtol=rtol, atol=0)
     assert_sets_match(kept, fix[f"{name}/idx"], attn_sum, text_max, thr, c["ithr"], 4 * rtol)
+
+
+@pytest.mark.parametrize("name", ITHR_CASES)
+def test_filter_oracle_rounds_individual_threshold(fix, name):
+    """A column whose maximum equals the threshold rounded to the stage dtype is kept, exactly as
+    the reference keeps it; the one just below is dropped (no tolerance: these columns sit on
+    the threshold by construction)."""
+    attn, c = load_case(fix, name)
+    kept, *_ = run_oracle(attn, c)
+    ref = set(fix[f"{name}/idx"].tolist())
+    assert [col in ref for col in ITHR_COLUMNS] == [True, False, True]
+    assert [col in set(kept.tolist()) for col in ITHR_COLUMNS] == [True, False, True]
+    np.testing.assert_array_equal(kept, fix[f"{name}/idx"])
 
 
 def test_stage_rounding():

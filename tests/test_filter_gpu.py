@@ -9,7 +9,8 @@ import pytest
 import torch
 
 from oracle import kv_oracle as ko
-from test_filter_golden import CASES, FIX, STAGE_RTOL, assert_sets_match, load_case, run_oracle
+from test_filter_golden import (CASES, FIX, ITHR_CASES, ITHR_COLUMNS, STAGE_RTOL, assert_sets_match, load_case,
+                                run_oracle)
 
 pytestmark = pytest.mark.gpu
 
@@ -30,6 +31,18 @@ def test_filter_matches_reference_and_oracle(built_lib, fix, name):
     kept, _, attn_sum, text_max, thr = run_oracle(attn, c)
     np.testing.assert_array_equal(got, kept)
     assert_sets_match(got, fix[f"{name}/idx"], attn_sum, text_max, thr, c["ithr"], 4 * STAGE_RTOL[c["stage"]])
+
+
+@pytest.mark.parametrize("name", ITHR_CASES)
+def test_filter_rounds_individual_threshold(built_lib, fix, name):
+    """The kernel rounds individual_thr to the stage dtype as torch does: the reference's kept set
+    exactly, the column sitting on the rounded threshold included."""
+    from mserve_b200.selection import dual_attention_filter
+    attn, c = load_case(fix, name)
+    got, _ = dual_attention_filter(attn.cuda(), c["start"], c["img"], c["gthr"], c["ithr"], use_fp16=c["fp16"])
+    got = got.cpu().numpy()
+    assert [col in set(got.tolist()) for col in ITHR_COLUMNS] == [True, False, True]
+    np.testing.assert_array_equal(got, fix[f"{name}/idx"])
 
 
 def _probabilities(H, T, seed):
