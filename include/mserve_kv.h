@@ -301,7 +301,8 @@ int mskv_sparse_attention(const mskv_attn_desc* d, void* stream);
  * MSKV_NOALLOC_ATTN_SCRATCH_BYTES built into the library, which each GPU that loads the
  * library holds until the process exits.  Shapes whose mskv_attention_workspace_bytes()
  * exceeds that size are rejected with MSKV_ERR_RANGE.  The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress) with that device current; make that
+ * the array's device address (cudaGetSymbolAddress) with that device current, and looks it up
+ * again when the device's context has been re-created since (cudaDeviceReset); make that
  * first call before any stream capture.  Every call on a device shares the array and
  * rewrites every part of it that it reads, so calls that overlap on the GPU -- on streams
  * not ordered with each other -- race and give wrong results.  Calls no cudaMalloc or

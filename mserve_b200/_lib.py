@@ -18,6 +18,9 @@ MSKV_ERR_DTYPE = 3
 MSKV_ERR_CUDA = 4
 MSKV_ERR_RANGE = 5
 
+# size of the device array behind mskv_sparse_attention_noalloc (MSKV_NOALLOC_ATTN_SCRATCH_BYTES)
+MSKV_NOALLOC_SCRATCH_BYTES = 8 << 20
+
 STATUS_INDEX_OOB = 0x1
 STATUS_BAD_PAGE = 0x2
 STATUS_DST_OOB = 0x4

@@ -537,16 +537,49 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
 // their own to hand out a workspace.  For them the split-sequence workspace lives in one
 // file-scope device array of MSKV_NOALLOC_ATTN_SCRATCH_BYTES, which every GPU that loads
 // this library keeps until the process exits.  Its device address is looked up once per
-// device (cudaGetSymbolAddress, on that device's first call) and cached; nothing is
-// allocated or freed.  Each call rewrites every partial it later reads, so nothing in the
-// array has to start at zero; but all calls on a device share it, so calls that overlap on
-// the GPU (different streams without ordering) race on it.
+// device (cudaGetSymbolAddress, on that device's first call) and cached together with the id
+// of the CUDA context it belongs to; a call from another context of that device (after a
+// cudaDeviceReset, or once the primary context was released and created again) looks the
+// address up again.  Nothing is allocated or freed.  Each call rewrites every partial it later
+// reads, so nothing in the array has to start at zero; but all calls on a device share it, so
+// calls that overlap on the GPU (different streams without ordering) race on it.
 static __device__ __align__(256) unsigned char g_attn_scratch[MSKV_NOALLOC_ATTN_SCRATCH_BYTES];
 
 namespace {
 constexpr int kMaxDevices = 64;
+struct ScratchAddr {
+  void* ptr;
+  unsigned long long ctx_id;   // 0: not looked up yet
+};
 std::mutex g_scratch_mu;
-void* g_scratch_dev[kMaxDevices] = {};
+ScratchAddr g_scratch_dev[kMaxDevices] = {};
+
+// Id of the calling thread's current CUDA context (driver API through the runtime's entry
+// point, so the library links only the runtime); 0 when there is none yet.
+unsigned long long current_context_id() {
+  using GetCurrent = int (*)(void**);
+  using GetId = int (*)(void*, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(f);
+    cudaGetLastError();
+  });
+  if (!get_current || !get_id) return 0;
+  void* ctx = nullptr;
+  if (get_current(&ctx) != 0 || !ctx) return 0;
+  unsigned long long id = 0;
+  return get_id(ctx, &id) == 0 ? id : 0;
+}
 
 int scratch_of_current_device(void** out) {
   int dev = 0;
@@ -554,13 +587,16 @@ int scratch_of_current_device(void** out) {
   if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(MSKV_ERR_RANGE, "device index %d beyond %d", dev, kMaxDevices);
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_dev[dev]) {
+  ScratchAddr& c = g_scratch_dev[dev];
+  const unsigned long long id = current_context_id();
+  if (!c.ptr || id == 0 || c.ctx_id != id) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);   // also creates the context if needed
     if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(attention scratch)");
-    g_scratch_dev[dev] = p;
+    c.ptr = p;
+    c.ctx_id = current_context_id();
   }
-  *out = g_scratch_dev[dev];
+  *out = c.ptr;
   return MSKV_OK;
 }
 }  // namespace

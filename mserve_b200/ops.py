@@ -60,22 +60,33 @@ def status_word(device: torch.device) -> torch.Tensor:
     return w
 
 
-def check_status(device: torch.device, what: str = "kernel") -> None:
-    """Synchronises the current stream, raises RuntimeError if any status bit is set, clears it."""
+def take_status(device: torch.device) -> int:
+    """Synchronises the current stream and returns the device status bits, clearing them."""
     w = status_word(device)
     v = int(w.item())
     if v:
         w.zero_()
-        reasons = []
-        if v & _lib.STATUS_INDEX_OOB:
-            reasons.append("token index out of range")
-        if v & _lib.STATUS_BAD_PAGE:
-            reasons.append("page-table entry not mapped")
-        if v & _lib.STATUS_DST_OOB:
-            reasons.append("destination token out of range")
-        if v & _lib.STATUS_TIMEOUT:
-            reasons.append("a wait for another GPU's flag timed out")
-        raise RuntimeError(f"{what}: {', '.join(reasons)} (status 0x{v:x}); offending rows were skipped")
+    return v
+
+
+def describe_status(v: int) -> str:
+    reasons = []
+    if v & _lib.STATUS_INDEX_OOB:
+        reasons.append("token index out of range")
+    if v & _lib.STATUS_BAD_PAGE:
+        reasons.append("page-table entry not mapped")
+    if v & _lib.STATUS_DST_OOB:
+        reasons.append("destination token out of range")
+    if v & _lib.STATUS_TIMEOUT:
+        reasons.append("a wait for another GPU's flag timed out")
+    return f"{', '.join(reasons)} (status 0x{v:x})"
+
+
+def check_status(device: torch.device, what: str = "kernel") -> None:
+    """Synchronises the current stream, raises RuntimeError if any status bit is set, clears it."""
+    v = take_status(device)
+    if v:
+        raise RuntimeError(f"{what}: {describe_status(v)}; offending rows were skipped")
 
 
 # ---------------------------------------------------------------------------------------

@@ -29,7 +29,7 @@ from typing import Dict, Optional, Tuple
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 
 def head_shard(kv_heads: int, world: int, rank: int) -> Tuple[int, int]:
@@ -75,8 +75,12 @@ class PeerExchange:
     The caller then reads the buffer (the top-k) on the same stream.  Two buffers make a
     separate "consumed" handshake unnecessary: a rank writes parity p again at epoch e + 2
     only after every rank signalled epoch e + 1, which each does after its stream finished
-    reading epoch e.  Every wait is bounded (timeout_s); expiry sets the timeout status bit,
-    which ops.check_status raises.  Every rank must make the same sequence of calls.
+    reading epoch e.  Every wait is bounded (timeout_s); expiry sets the timeout status bit and
+    lets the stream go on.  A wait that expired breaks the two-buffer argument (a lagging peer
+    may still be writing into the buffer being read), so check_status(), which reads the
+    status bits, marks the exchange unusable when it finds that bit: every later score() raises,
+    and the exchange must be closed and created again.  Every rank must make the same sequence
+    of calls.
     """
 
     def __init__(self, batch: int, local_heads: int, max_tokens: int, *, group=None,
@@ -110,6 +114,16 @@ class PeerExchange:
                       for p in (0, 1)]
         self.epoch = 0
         self.closed = False
+        self.broken = False
+
+    def check_status(self, what: str = "peer exchange") -> None:
+        """Waits for this rank's stream, then raises RuntimeError if a kernel reported a status
+        bit; a timed-out wait also marks the exchange unusable (see the class docstring)."""
+        v = self.ops.take_status(self.device)
+        if v & _lib.STATUS_TIMEOUT:
+            self.broken = True
+        if v:
+            raise RuntimeError(f"{what}: {self.ops.describe_status(v)}")
 
     def _rows_at(self, r: int, parity: int) -> int:
         """Address of this rank's block in parity `parity` of rank r's buffer."""
@@ -119,6 +133,11 @@ class PeerExchange:
         """Scores this rank's heads into every rank's buffer; returns this rank's complete
         [world, B, Hl, T] buffer of the new epoch, to be read on the current stream before the
         next call's score kernel (which follows on the same stream)."""
+        if self.broken:
+            raise RuntimeError("peer exchange unusable: a wait for another rank's scores timed out; "
+                               "close() it and create a new one")
+        if self.closed:
+            raise RuntimeError("peer exchange is closed")
         W, e = self.world, self.epoch + 1
         p = e % 2
         _, B, Hl, T = self.shape
@@ -204,6 +223,14 @@ class SharedSelection:
                        rows_per_sel=self.Hkv, sel_per_batch=1, scale=scale, out=out, counts=counts,
                        out_dtype=out_dtype, row_blocks=(self.world, self.B, self.Hl))
         return res
+
+    def check_status(self, what: str = "shared selection") -> None:
+        """Raises RuntimeError if a kernel of this rank reported a status bit (synchronising); with
+        exchange='peer' a timed-out wait leaves the selection unusable until it is recreated."""
+        if self.peer is not None:
+            self.peer.check_status(what)
+        else:
+            ops.check_status(self.device, what)
 
     def close(self) -> None:
         """Releases the peer exchange's memory (collective with exchange='peer')."""

@@ -10,7 +10,10 @@ build output goes to oracle/_ref/ only, which travels to the GPU machine with th
 Users: tests/test_reference_kernel_gpu.py (bit-exact cross-check of mskv_uva_gather against
 the reference kernel) and oracle/time_reference_kernel.py (the reference kernel's gather rate).
 
-    python -m oracle.build_ref [--force]
+    python -m oracle.build_ref [--force] [--reference <MServe checkout>]
+
+The reference checkout comes from --reference or the MSERVE_REFERENCE environment variable;
+without either, an existing build is kept and nothing is compiled.
 """
 from __future__ import annotations
 
@@ -22,15 +25,25 @@ import sysconfig
 from pathlib import Path
 from typing import Optional
 
-REF_SOURCE = Path("/root/reference/qwen-eljrte/cuda_uva_kernel.cpp")
+REF_FILE = "qwen-eljrte/cuda_uva_kernel.cpp"
 OUT_DIR = Path(__file__).resolve().parent / "_ref"
 OUT = OUT_DIR / "cuda_uva_ref.so"
 MODULE = "cuda_uva_ref"
 
 
-def build(force: bool = False) -> Optional[Path]:
+def reference_source(reference: Optional[str] = None) -> Optional[Path]:
+    """The reference kernel source under `reference` (default: $MSERVE_REFERENCE), if present."""
+    root = reference or os.environ.get("MSERVE_REFERENCE")
+    if not root:
+        return None
+    src = Path(root) / REF_FILE
+    return src if src.exists() else None
+
+
+def build(force: bool = False, reference: Optional[str] = None) -> Optional[Path]:
     """Returns the built module path, or None when neither the source nor a build exists."""
-    if not REF_SOURCE.exists():
+    REF_SOURCE = reference_source(reference)
+    if REF_SOURCE is None:
         return OUT if OUT.exists() else None
     if OUT.exists() and not force and OUT.stat().st_mtime >= REF_SOURCE.stat().st_mtime:
         return OUT
@@ -66,4 +79,9 @@ def load():
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv))
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--reference", default=None, help="root of an MServe checkout (default: $MSERVE_REFERENCE)")
+    a = ap.parse_args()
+    print(build(force=a.force, reference=a.reference))

@@ -1,8 +1,9 @@
 """Generates tests/golden/reference_vectors.npz by running MServe's own Python code on CPU.
 
-Run in a container that has the reference checked out (default /root/reference):
+Run where the reference is checked out:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <MServe checkout>
+    (or MSERVE_REFERENCE=<MServe checkout> python tests/golden/make_golden.py)
 
 What is executed (unmodified reference source, CPU tensors):
   * compute_token_importance, sparse_sdpa_attention, repeat_kv
@@ -20,6 +21,7 @@ read the reference tree.
 from __future__ import annotations
 
 import argparse
+import os
 import ast
 import contextlib
 import math
@@ -111,9 +113,12 @@ def load_index_generator(ref: Path):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("MSERVE_REFERENCE"),
+                    help="root of an MServe checkout (default: $MSERVE_REFERENCE)")
     ap.add_argument("--out", default=str(HERE / "reference_vectors.npz"))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set MSERVE_REFERENCE to the root of an MServe checkout")
     ref = Path(args.reference)
     fx = load_attention_functions(ref)
     out: dict = {}

@@ -116,6 +116,7 @@ class _SharedMemoryBackend:
         self.rank = rank
         self.segs = {}                  # base -> (SharedMemory, size)
         self.next = (rank + 1) << 40
+        self.status = 0                 # the device status word
 
     def _register(self, shm, size):
         base = self.next
@@ -172,8 +173,16 @@ class _SharedMemoryBackend:
         t0 = time.monotonic()
         while not all((x >= value) if at_least else (x == value) for x in v):
             if time.monotonic() - t0 > timeout_s:
-                raise TimeoutError(f"flags {list(v)} did not reach {value}")
+                self.status |= 0x8      # as the device wait does: a status bit, and go on
+                return
             time.sleep(0.0005)
+
+    def take_status(self, device):
+        v, self.status = self.status, 0
+        return v
+
+    def describe_status(self, v):
+        return f"status 0x{v:x}"
 
 
 def _peer_worker(rank, world, port, epochs):
@@ -213,3 +222,38 @@ def test_peer_exchange_protocol(world):
     epoch's gathered buffer holds every rank's rows of that epoch (none of another epoch),
     while ranks drift apart and read their buffers late by random delays."""
     mp.start_processes(_peer_worker, args=(world, _free_port(), 7), nprocs=world, join=True, start_method="spawn")
+
+
+def _timeout_worker(rank, world, port):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from mserve_b200 import parallel
+        B, Hq, Hkv, T, D = 2, 8, 4, 50, 16
+        Hl, G = Hkv // world, Hq // Hkv
+        be = _SharedMemoryBackend(rank)
+        ex = parallel.PeerExchange(B, Hl, T, device=torch.device("cpu"), timeout_s=0.3, backend=be)
+        q, k = _case(7, B=B, Hq=Hq, Hkv=Hkv, T=T, D=D)
+        h0, h1 = rank * Hl, (rank + 1) * Hl
+        ex.score(q[:, h0 * G:h1 * G], k[:, h0:h1], max_tokens=T)           # epoch 1: every rank
+        ex.check_status()
+        if rank == 0:                                                       # epoch 2: rank 1 never joins
+            ex.score(q[:, h0 * G:h1 * G], k[:, h0:h1], max_tokens=T)
+            with pytest.raises(RuntimeError, match="0x8"):
+                ex.check_status()
+            assert ex.broken
+            with pytest.raises(RuntimeError, match="unusable"):
+                ex.score(q[:, h0 * G:h1 * G], k[:, h0:h1], max_tokens=T)
+        else:
+            assert not ex.broken
+        ex.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_timeout_leaves_it_unusable():
+    """A rank that never joins an epoch: the other rank's bounded wait expires, check_status()
+    raises on the timeout bit and every later score() refuses to run until the exchange is
+    recreated (a lagging peer could still write into the buffer being read)."""
+    mp.start_processes(_timeout_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")

@@ -1,7 +1,8 @@
 """Parity of scoring (mskv_score) and selection (mskv_topk) with the oracle.
 
-Scores: fp32 on the GPU vs fp64 in the oracle, within 1e-3 relative (scaled by the score
-magnitude).  Selection: bit-exact index sets when the oracle ranks the GPU's own fp32 scores;
+Scores: fp32 on the GPU vs fp64 in the oracle, within 1e-3 relative; only scores smaller than a
+tenth of the mean magnitude (where a dot product cancels and its relative error means nothing)
+are held to the absolute bound that 1e-3 gives at that size.  Selection: bit-exact index sets when the oracle ranks the GPU's own fp32 scores;
 against the reference's golden outputs, index sets equal except at (near-)ties.
 """
 import numpy as np
@@ -16,10 +17,16 @@ pytestmark = pytest.mark.gpu
 SCORE_RTOL = 1e-3
 
 
+def scores_close_error(got: np.ndarray, ref: np.ndarray) -> float:
+    """max |got - ref| / max(|ref|, mean|ref| / 10): the relative error of every score except
+    the near-zero ones, which are measured against a tenth of the mean magnitude."""
+    floor = 0.1 * np.abs(ref).mean() + 1e-30
+    return float((np.abs(got.astype(np.float64) - ref) / np.maximum(np.abs(ref), floor)).max())
+
+
 def _assert_scores_close(got: np.ndarray, ref: np.ndarray):
-    scale = np.abs(ref).mean() + 1e-30
-    err = np.abs(got.astype(np.float64) - ref) / (np.abs(ref) + scale)
-    assert err.max() <= SCORE_RTOL, f"max scaled error {err.max():.3e}"
+    err = scores_close_error(got, ref)
+    assert err <= SCORE_RTOL, f"max relative error {err:.3e}"
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])

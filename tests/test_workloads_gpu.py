@@ -19,6 +19,7 @@ import pytest
 import torch
 
 from conftest import to_numpy_bits
+from test_select_gpu import scores_close_error
 from oracle import kv_oracle as ko
 
 pytestmark = pytest.mark.gpu
@@ -38,7 +39,7 @@ def _check_layer(eng, layer, q, ks, vs, lens, top_k, recent):
         L = lens[b]
         ref = ko.gqa_scores(qn[b:b + 1], ks[b].float().numpy()[None])[0]
         s = scores[b, :, :L].astype(np.float64)
-        assert (np.abs(s - ref) / (np.abs(ref) + np.abs(ref).mean())).max() < 1e-3, f"scores of sequence {b}"
+        assert scores_close_error(s, ref) < 1e-3, f"scores of sequence {b}"
     # 2. selection: the oracle's rule on the GPU's fp32 scores
     sel, rcnt = ko.select_topk_window(scores.reshape(B * Hkv, -1), top_k=top_k, recent=recent,
                                       lens=np.asarray(lens), sel_per_batch=Hkv)
