@@ -12,10 +12,14 @@ Same constructor, method names, arguments and return values; different mechanics
   bound is kept: at most ``queue_maxsize`` appends may be in flight, beyond that the call
   returns False (block=False) or waits up to timeout_ms (block=True), as the reference's
   queue.Queue does (kv_cache.py:682-702);
-* ``get_sparse_async_uva`` / ``get_sparse_async`` gather the selected rows with the sm_100a
-  gather kernel on the caller's current stream, without the reference's
-  torch.cuda.synchronize() (kv_cache.py:531).  There is no CPU index_select fallback: both
-  names run the same kernel;
+* ``get_sparse_async_uva`` gathers the selected rows with the sm_100a gather kernel into new
+  tensors on the caller's current stream, without the reference's torch.cuda.synchronize()
+  (kv_cache.py:531); ``get_sparse_async`` runs the same kernel into reusable per-layer device
+  buffers on the cache's own copy stream and returns views of them with that stream's event,
+  as the reference's index_select + H2D path does (kv_cache.py:576-629).  There is no CPU
+  index_select path;
+* ``get_full_kv`` concatenates CUDA tensors with the row-copy kernel (two launches into one new
+  tensor per K and V), as torch.cat does in the reference (kv_cache.py:631-643);
 * indices are bounds-checked: a token index >= the cached length raises RuntimeError (the
   reference reads past the host tensor when the selection includes the token being
   decoded, attention.py:1953-1967).
@@ -45,6 +49,27 @@ class _Layer:
         self.pending: List[torch.cuda.Event] = []
         self.start_dev = {}     # device index -> (start, int32 [B] device tensor of it)
         self.lock = threading.Lock()
+
+
+def _cat_tokens(old: torch.Tensor, new: torch.Tensor) -> torch.Tensor:
+    """[B, H, T, D] ++ [B, H, n, D] along tokens on the GPU with two row-copy launches."""
+    if old.dim() != 4 or new.dim() != 4 or old.shape[:2] != new.shape[:2] or old.shape[3] != new.shape[3]:
+        raise RuntimeError(f"Sizes of tensors must match except in dimension 2: {tuple(old.shape)} vs "
+                           f"{tuple(new.shape)}")
+    if old.dtype != new.dtype or old.device != new.device:
+        raise RuntimeError("get_full_kv: past and new KV must share dtype and device")
+    B, H, T, D = old.shape
+    n = new.shape[2]
+    out = torch.empty(B, H, T + n, D, dtype=old.dtype, device=old.device)
+    for src, lo, cnt in ((old, 0, T), (new, T, n)):
+        if cnt == 0 or B * H * D == 0:
+            continue
+        if src.stride(3) != 1:
+            src = src.contiguous()
+        ops.copy_rows(ops.strided_rows(src, device=src.device),
+                      ops.strided_rows(out[:, :, lo:lo + cnt], device=out.device),
+                      batch=B, num_tokens=cnt, device=out.device)
+    return out
 
 
 class CPUKVCache:
@@ -195,20 +220,44 @@ class CPUKVCache:
 
         token_indices: int64 [S] on the CPU (the reference contract) or an int32/int64 CUDA
         tensor [S], [B, S] or [B, H, S].  Returns (k [B, H, S, D], v, done_event) or None if
-        the layer is empty.
+        the layer is empty.  The gather runs on the caller's current stream.
         """
-        layer = self._layers[layer_idx]
-        if layer is None:
-            return None
+        dev = self._cuda_device(device)
+        return self._gather(layer_idx, dev, token_indices, torch.cuda.current_stream(dev), reuse=False)
+
+    @staticmethod
+    def _cuda_device(device) -> torch.device:
         dev = torch.device(device)
         if dev.type != "cuda":
             raise ValueError("device must be a CUDA device")
         if dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
+        return dev
+
+    def _sparse_buffers(self, layer_idx: int, layer: _Layer, dev: torch.device, S: int):
+        """Reusable device buffers of the layer, keyed (layer, B, H, D, dtype, device) and grown
+        to the largest S asked for, as the reference keys its GPU buffers (kv_cache.py:604-620)."""
+        if not hasattr(self, "_sparse_gpu_buffers"):
+            self._sparse_gpu_buffers = {}
+        key = (layer_idx, layer.B, layer.H, layer.D, layer.dtype, dev.index)
+        buf = self._sparse_gpu_buffers.get(key)
+        if buf is None or buf[0].shape[2] < S:
+            kb = torch.empty(layer.B, layer.H, max(S, 1), layer.D, dtype=layer.dtype, device=dev)
+            buf = (kb, torch.empty_like(kb))
+            self._sparse_gpu_buffers[key] = buf
+        return buf
+
+    def _gather(self, layer_idx: int, dev: torch.device, token_indices: torch.Tensor, stream: torch.cuda.Stream,
+                reuse: bool):
+        layer = self._layers[layer_idx]
+        if layer is None:
+            return None
         cur = torch.cuda.current_stream(dev)
+        if stream != cur:
+            stream.wait_stream(cur)       # the indices and any earlier use of the buffers
         for e in layer.pending:           # order after in-flight write-backs of this layer
-            cur.wait_event(e)
-        with layer.lock:
+            stream.wait_event(e)
+        with layer.lock, torch.cuda.stream(stream):
             T, start = layer.len, layer.start
             if token_indices.device.type == "cpu":
                 idx = token_indices.to(torch.int64)
@@ -228,22 +277,35 @@ class CPUKVCache:
                     idx = idx.to(torch.int64)
             idx = idx.contiguous()
             S = idx.shape[-1]
-            k_out = torch.empty(layer.B, layer.H, S, layer.D, dtype=layer.dtype, device=dev)
-            v_out = torch.empty_like(k_out)
+            if reuse:
+                kb, vb = self._sparse_buffers(layer_idx, layer, dev, S)
+                k_out, v_out = kb[:, :, :S], vb[:, :, :S]
+            else:
+                k_out = torch.empty(layer.B, layer.H, S, layer.D, dtype=layer.dtype, device=dev)
+                v_out = torch.empty_like(k_out)
             start_t = self._start_tensor(layer, dev)
-            start_t.record_stream(cur)      # the cached tensor may be replaced while this runs
+            start_t.record_stream(stream)   # the cached tensor may be replaced while this runs
             src = ops.strided_rows(layer.k, layer.v, len_scalar=T, ring_start=start_t, ring_cap=self.max_len,
                                    device=dev)
             ops.gather(src, idx, k_out, v_out, batch=layer.B)
-        done = torch.cuda.Event()
-        done.record(cur)
-        idx.record_stream(cur)
+            done = torch.cuda.Event()
+            done.record(stream)
+        idx.record_stream(stream)
         return k_out, v_out, done
 
     def get_sparse_async(self, layer_idx: int, device: torch.device, token_indices: torch.Tensor):
-        """Same result as get_sparse_async_uva (kv_cache.py:545-629).  The reference's CPU
-        index_select + H2D path is replaced by the device gather; no CPU path exists."""
-        return self.get_sparse_async_uva(layer_idx, device, token_indices)
+        """The selected tokens in reusable device buffers (kv_cache.py:545-629).
+
+        Same arguments and result values as get_sparse_async_uva.  As in the reference, the rows
+        land in per-layer GPU buffers that the next call for the same layer (and shape)
+        overwrites, the copy runs on the cache's own stream (ordered after the caller's current
+        stream), and the returned event is recorded on that stream: wait on it before reading.
+        The reference's CPU index_select into pinned buffers + H2D copy is replaced by the
+        device gather straight from the host store; no CPU path exists.
+        """
+        dev = self._cuda_device(device)
+        stream = self._h2d_stream if dev == self.device else torch.cuda.Stream(device=dev)
+        return self._gather(layer_idx, dev, token_indices, stream, reuse=True)
 
     def check_errors(self) -> None:
         """Raises if a gather met an out-of-range device index (synchronises)."""
@@ -298,11 +360,19 @@ class CPUKVCache:
     @staticmethod
     def get_full_kv(past_key_value: Optional[Tuple[torch.Tensor, torch.Tensor]], key_new: torch.Tensor,
                     value_new: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-        """cat(past, new) along tokens (kv_cache.py:631-643)."""
+        """cat(past, new) along the token axis (kv_cache.py:631-643): [B, H, T, D] + [B, H, n, D]
+        -> new tensors [B, H, T + n, D].
+
+        For CUDA tensors the rows are moved by the row-copy kernel (mskv_copy_rows: the past
+        rows, then the new ones behind them, on the current stream; any strides with a
+        contiguous head_dim).  Host tensors are concatenated by torch, as in the reference.
+        """
         if past_key_value is None:
             return key_new, value_new
         k_old, v_old = past_key_value
-        return torch.cat([k_old, key_new], dim=2), torch.cat([v_old, value_new], dim=2)
+        if not all(t.is_cuda for t in (k_old, v_old, key_new, value_new)):
+            return torch.cat([k_old, key_new], dim=2), torch.cat([v_old, value_new], dim=2)
+        return _cat_tokens(k_old, key_new), _cat_tokens(v_old, value_new)
 
     def shutdown(self, wait: bool = False, drain: bool = True, timeout_s: Optional[float] = None) -> None:
         """Drains in-flight appends (drain=True) and refuses further appends (kv_cache.py:769-781)."""

@@ -259,6 +259,16 @@ def sparse_sdpa_attention(q: np.ndarray, k_sel: np.ndarray, v_sel: np.ndarray, *
 # ---------------------------------------------------------------------------------------
 
 
+def full_kv(past: Optional[Tuple[np.ndarray, np.ndarray]], new_k: np.ndarray, new_v: np.ndarray
+            ) -> Tuple[np.ndarray, np.ndarray]:
+    """CPUKVCache.get_full_kv (qwen-eljrte/Qwen_Transformer/kv_cache.py:631-643): the past K/V
+    [B, H, T, D] followed by the new rows [B, H, n, D] along the token axis; no past: the new
+    rows themselves."""
+    if past is None:
+        return new_k, new_v
+    return (np.concatenate([past[0], new_k], axis=2), np.concatenate([past[1], new_v], axis=2))
+
+
 def cat_truncate(old_k: Optional[np.ndarray], old_v: Optional[np.ndarray], new_k: np.ndarray, new_v: np.ndarray,
                  max_len: int) -> Tuple[np.ndarray, np.ndarray]:
     """Host-cache append: cat along tokens, keep the last max_len.

@@ -144,3 +144,72 @@ def test_page_writeback_to_host(built_lib):
                       counts.numpy(), ring_start=ring.numpy(), ring_cap=C)
     np.testing.assert_array_equal(to_numpy_bits(host_k), ek)
     np.testing.assert_array_equal(to_numpy_bits(host_v), ev)
+
+
+def test_get_sparse_async_matches_reference_golden(built_lib, golden):
+    """get_sparse_async (kv_cache.py:545-629): the rows land in the cache's reusable per-layer
+    device buffers, copied on its own stream, and equal the reference's own get_sparse_async
+    output on the golden cache; later calls with more and fewer indices reuse (and grow) the
+    buffers and stay bit-exact with the oracle."""
+    from mserve_b200.kv_cache import CPUKVCache
+    k = from_bits(golden["sparse/k"], torch.bfloat16)
+    v = from_bits(golden["sparse/v"], torch.bfloat16)
+    B, H, T, D = k.shape
+    cache = CPUKVCache(num_layers=2, max_len=T + 16)
+    assert cache.submit_append(1, k.cuda(), v.cuda())
+    idx = torch.from_numpy(golden["sparse/idx"])
+    ks, vs, ev = cache.get_sparse_async(1, torch.device("cuda"), idx)
+    assert ks.shape == (B, H, idx.numel(), D)
+    torch.cuda.current_stream().wait_event(ev)
+    np.testing.assert_array_equal(to_numpy_bits(ks), golden["sparse/k_sel"].view(np.int16))
+    np.testing.assert_array_equal(to_numpy_bits(vs), golden["sparse/v_sel"].view(np.int16))
+    kb = to_numpy_bits(k)
+    vb = to_numpy_bits(v)
+    g = torch.Generator().manual_seed(5)
+    storages = []
+    for S, on_gpu in ((3 * idx.numel(), False), (7, True), (idx.numel() + 1, False)):
+        sel = torch.randint(0, T, (S,), generator=g)
+        ks2, vs2, ev2 = cache.get_sparse_async(1, torch.device("cuda"), sel.cuda() if on_gpu else sel)
+        torch.cuda.current_stream().wait_event(ev2)
+        ek, evv = ko.index_select_gather(kb, vb, sel.numpy())
+        np.testing.assert_array_equal(to_numpy_bits(ks2), ek)
+        np.testing.assert_array_equal(to_numpy_bits(vs2), evv)
+        storages.append(ks2.untyped_storage().data_ptr())
+    # once grown to the largest selection, later calls of the layer reuse the same buffer
+    assert storages[0] == storages[1] == storages[2]
+    assert ks2.untyped_storage().nbytes() >= B * H * 3 * idx.numel() * D * 2
+    with pytest.raises(RuntimeError, match="out of range"):
+        cache.get_sparse_async(1, torch.device("cuda"), torch.tensor([T]))
+    assert cache.get_sparse_async(0, torch.device("cuda"), idx) is None
+    cache.shutdown()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32, torch.float8_e4m3fn])
+def test_get_full_kv_matches_oracle(built_lib, dtype):
+    """get_full_kv (kv_cache.py:631-643) on CUDA tensors runs the row-copy kernel: bit-exact with
+    the oracle's concatenation for contiguous and strided past/new tensors and empty parts."""
+    from mserve_b200.kv_cache import CPUKVCache
+    g = torch.Generator().manual_seed(11)
+
+    def rnd(*shape):
+        return (torch.randn(*shape, generator=g) * 3).to(dtype).cuda()
+    B, H, T, n, D = 2, 4, 300, 5, 128
+    cases = [
+        ((rnd(B, H, T, D), rnd(B, H, T, D)), rnd(B, H, n, D), rnd(B, H, n, D)),
+        # strided views: a token slice of a larger cache, and a [B, T, H, D] tensor seen as [B, H, T, D]
+        ((rnd(B, H, T + 40, D)[:, :, 17:17 + T], rnd(B, T, H, D).transpose(1, 2)), rnd(B, H, n, D),
+         rnd(B, n, H, D).transpose(1, 2)),
+        ((rnd(B, H, 0, D), rnd(B, H, 0, D)), rnd(B, H, 1, D), rnd(B, H, 1, D)),
+        ((rnd(B, H, T, D), rnd(B, H, T, D)), rnd(B, H, 0, D), rnd(B, H, 0, D)),
+    ]
+    for past, kn, vn in cases:
+        k, v = CPUKVCache.get_full_kv(past, kn, vn)
+        torch.cuda.synchronize()
+        ek, ev = ko.full_kv((to_numpy_bits(past[0]), to_numpy_bits(past[1])), to_numpy_bits(kn), to_numpy_bits(vn))
+        assert k.is_cuda and k.is_contiguous() and k.dtype == dtype
+        np.testing.assert_array_equal(to_numpy_bits(k), ek)
+        np.testing.assert_array_equal(to_numpy_bits(v), ev)
+    k, v = CPUKVCache.get_full_kv(None, kn, vn)
+    assert k is kn and v is vn
+    with pytest.raises(RuntimeError, match="Sizes of tensors must match"):
+        CPUKVCache.get_full_kv((rnd(B, H, T, D), rnd(B, H, T, D)), rnd(B, H + 1, n, D), rnd(B, H + 1, n, D))

@@ -79,3 +79,20 @@ def test_cpulist_parsing():
     from mserve_b200 import topology
     assert topology.parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
     assert topology.parse_cpulist("") == set()
+
+
+def test_cuda_uva_module_imports_by_name(built_lib):
+    """The torch extension answers to the reference's module name and signature, and checks its
+    arguments before any GPU work (unpinned host KV raises the reference's error text)."""
+    import subprocess
+    import sys
+    from mserve_b200 import build
+    ext = build.build_torch_ext()
+    code = ("import sys, torch; sys.path.insert(0, %r); import cuda_uva; "
+            "assert cuda_uva.__file__ == %r; "
+            "k = torch.zeros(1, 1, 4, 8)\n"
+            "try:\n    cuda_uva.uva_gather(k, k, torch.tensor([0]), 1, 1, 4, 8)\n"
+            "except RuntimeError as e:\n    print(str(e).splitlines()[0])\n") % (str(ext.parent), str(ext))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "k_in must be pinned memory for UVA" in out.stdout

@@ -72,3 +72,20 @@ def test_reference_arm_json_line():
     cb = line["cpu_baseline"]
     assert cb["value"] == line["value"] and cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_get_full_kv_host_tensors_and_oracle():
+    """get_full_kv on host tensors is torch.cat, as in the reference (kv_cache.py:631-643); the
+    oracle's restatement gives the same arrays; with no past the new rows come back as they are."""
+    import numpy as np
+    import torch
+    from oracle import kv_oracle as ko
+    from mserve_b200.kv_cache import CPUKVCache
+    g = torch.Generator().manual_seed(2)
+    past = (torch.randn(2, 3, 9, 16, generator=g), torch.randn(2, 3, 9, 16, generator=g))
+    kn, vn = torch.randn(2, 3, 4, 16, generator=g), torch.randn(2, 3, 4, 16, generator=g)
+    k, v = CPUKVCache.get_full_kv(past, kn, vn)
+    ek, ev = ko.full_kv((past[0].numpy(), past[1].numpy()), kn.numpy(), vn.numpy())
+    np.testing.assert_array_equal(k.numpy(), ek)
+    np.testing.assert_array_equal(v.numpy(), ev)
+    assert CPUKVCache.get_full_kv(None, kn, vn) == (kn, vn)
