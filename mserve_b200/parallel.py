@@ -1,7 +1,9 @@
 """KV heads sharded over the GPUs of one node.
 
 One process per GPU; rank r holds the KV heads [r*Hl, (r+1)*Hl) of every sequence, Hl =
-Hkv / world, in its own host store, and gathers them over its own host link.
+Hkv / world, in its own host store, and gathers them over its own host link.  With more ranks
+than KV heads the sequences are split too (shard_plan): every (sequence, KV head) pair lives on
+exactly one rank.
 
 * Per-(sequence, KV head) selection (the recent-window top-k) needs no exchange: each rank
   scores, selects, gathers and attends its own heads, and nothing crosses NVLink.
@@ -24,6 +26,7 @@ head), never KV rows.  Two forms:
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -40,6 +43,49 @@ def head_shard(kv_heads: int, world: int, rank: int) -> Tuple[int, int]:
         raise ValueError(f"{kv_heads} KV heads do not split evenly over {world} ranks")
     hl = kv_heads // world
     return rank * hl, (rank + 1) * hl
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    """The (sequence, KV head) block of one rank when `world` ranks split one decode problem of
+    `batch` sequences x `kv_heads` KV heads.  The KV heads are split first (head_groups =
+    min(world, kv_heads) groups of kv_heads / head_groups heads); when there are more ranks than
+    KV heads, the sequences are split as well (seq_groups = world / head_groups groups).  Rank r
+    holds heads [h0, h1) of sequences [b0, b1) with head group r % head_groups and sequence
+    group r // head_groups, so the ranks of one sequence group are consecutive and hold its
+    heads in order -- the process group of a shared selection over those heads."""
+    world: int
+    rank: int
+    head_groups: int
+    seq_groups: int
+    b0: int
+    b1: int
+    h0: int
+    h1: int
+
+    @property
+    def seq_group(self) -> int:
+        return self.rank // self.head_groups
+
+    def group_ranks(self, seq_group: int):
+        """Global ranks of one sequence group, in head order."""
+        return list(range(seq_group * self.head_groups, (seq_group + 1) * self.head_groups))
+
+
+def shard_plan(batch: int, kv_heads: int, world: int, rank: int) -> ShardPlan:
+    """Splits batch x kv_heads (sequence, KV head) pairs evenly over `world` ranks (see ShardPlan)."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of world {world}")
+    hg = min(world, kv_heads)
+    if kv_heads % hg or world % hg:
+        raise ValueError(f"{world} ranks cannot split {kv_heads} KV heads evenly")
+    sg = world // hg
+    if batch % sg:
+        raise ValueError(f"{world} ranks over {kv_heads} KV heads leave {sg} sequence groups, which do not "
+                         f"split {batch} sequences evenly")
+    hl, bl = kv_heads // hg, batch // sg
+    hi, si = rank % hg, rank // hg
+    return ShardPlan(world, rank, hg, sg, si * bl, (si + 1) * bl, hi * hl, (hi + 1) * hl)
 
 
 def exchange_head_scores(local: torch.Tensor, gathered: torch.Tensor, group=None) -> torch.Tensor:

@@ -59,8 +59,8 @@ def test_reference_arm_json_line():
 
     import bench
     root = Path(bench.__file__).resolve().parent
-    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0"],
-                       cwd=root, capture_output=True, text=True, timeout=600)
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0",
+                        "--layers", "2"], cwd=root, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
     assert len(lines) == 1
@@ -68,9 +68,15 @@ def test_reference_arm_json_line():
     assert line["impl"] == "reference" and line["metric"] == bench.METRIC
     assert line["unit"] == "GB/s" and line["higher_is_better"] is True and line["value"] > 0
     assert line["n_gpus"] == 1 and line["steps"] == 1 and line["warmup"] == 0
-    assert line["config"]["workload"] == bench.WORKLOADS["qwen7b"][1]
+    wl = dict(bench.WORKLOADS["qwen7b"][0], layers=2)
+    name = bench.WORKLOADS["qwen7b"][1]
+    # the same config as the product arm prints at this N
+    assert line["config"] == bench.workload_config(wl, name, 1, bench.plan_description(wl, 1))
+    assert line["scaling"] == "strong"
     cb = line["cpu_baseline"]
     assert cb["value"] == line["value"] and cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
+    assert "every one of the 2 layers" in cb["sample"]
+    assert cb["index_select_gather_gbs"]["threads_1"] > 0 and len(cb["index_select_gather_gbs"]) == 2
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 

@@ -257,3 +257,34 @@ def test_peer_exchange_timeout_leaves_it_unusable():
     raises on the timeout bit and every later score() refuses to run until the exchange is
     recreated (a lagging peer could still write into the buffer being read)."""
     mp.start_processes(_timeout_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+
+
+@pytest.mark.parametrize("B,Hkv,world", [(8, 4, 1), (8, 4, 2), (8, 4, 4), (8, 4, 8), (16, 8, 8), (32, 8, 4),
+                                         (2, 1, 2)])
+def test_shard_plan_covers_every_pair_once(B, Hkv, world):
+    """Every (sequence, KV head) pair on exactly one rank; heads split before sequences; the
+    ranks of a sequence group are consecutive and hold its heads in order."""
+    from mserve_b200.parallel import shard_plan
+    owner = {}
+    for r in range(world):
+        p = shard_plan(B, Hkv, world, r)
+        assert p.head_groups == min(world, Hkv) and p.head_groups * p.seq_groups == world
+        assert (p.b1 - p.b0) * (p.h1 - p.h0) * world == B * Hkv
+        ranks = p.group_ranks(p.seq_group)
+        assert r in ranks and ranks == sorted(ranks)
+        assert [shard_plan(B, Hkv, world, q).h0 for q in ranks] == sorted(shard_plan(B, Hkv, world, q).h0 for q in ranks)
+        for b in range(p.b0, p.b1):
+            for h in range(p.h0, p.h1):
+                assert (b, h) not in owner
+                owner[(b, h)] = r
+    assert len(owner) == B * Hkv
+
+
+def test_shard_plan_rejects_uneven_splits():
+    from mserve_b200.parallel import shard_plan
+    with pytest.raises(ValueError):
+        shard_plan(8, 4, 3, 0)          # 3 ranks over 4 heads
+    with pytest.raises(ValueError):
+        shard_plan(7, 4, 8, 0)          # 8 ranks over 4 heads: 2 sequence groups of 7 sequences
+    with pytest.raises(ValueError):
+        shard_plan(8, 4, 8, 8)
