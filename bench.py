@@ -97,6 +97,8 @@ def parse():
     ap.add_argument("--no-exchange", action="store_true", help="skip the shared-selection exchange timing")
     ap.add_argument("--no-parity", action="store_true", help="skip the per-rank check against the unsharded layer")
     ap.add_argument("--chunks", type=int, default=4, help="sequence chunks pipelined per layer")
+    ap.add_argument("--gather-ctas", type=int, default=0,
+                    help="CTAs of each host-memory gather (0: the library's default bound)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen7b",
                     help="qwen7b (the headline workload), qwen32b (64 layers need ~140 GB of pinned host memory "
                          "in all: use --layers on smaller hosts) or llava34b")
@@ -168,16 +170,27 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        """Starts sampling every 50 ms and returns once the first sample is in (at most 3 s), so
+        the samples cover the work that follows."""
+        self.lines = []
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.idx), "-lms", "100"], stdout=subprocess.PIPE,
+                                          "-i", str(self.idx), "-lms", "50"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
+            return self
+        import selectors
+        sel = selectors.DefaultSelector()
+        sel.register(self.proc.stdout, selectors.EVENT_READ)
+        if sel.select(timeout=3.0):
+            first = self.proc.stdout.readline()
+            if first.strip():
+                self.lines.append(first)
+        sel.close()
         return self
 
     def __exit__(self, *a):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -185,7 +198,7 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.lines += [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -725,6 +738,7 @@ def run_mserve(args, world, rank, local):
     L = wl["layers"]
     plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank)
     eng, q = build_engine(wl, plan, dev)
+    eng.host_link_ctas = args.gather_ctas
     turn = None
     if wl.get("turn_image", 0) + wl.get("turn_text", 0):
         ms, host_bytes, page_bytes = append_turn(eng, wl, plan, dev)
@@ -752,14 +766,16 @@ def run_mserve(args, world, rank, local):
     n0 = _lib.launch_count()
     graph = eng.capture_decode_step(q, out_all, chunks=args.chunks)
     kernels_per_step = (_lib.launch_count() - n0) // 2     # warm-up run + captured run
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize(dev)
-    ops.check_status(dev, "bench warm-up")
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize(dev)
+    # clocks sampled from the warm-up through the timed region (a short timed region alone can
+    # end before nvidia-smi's first sample)
     with ClockSampler(local) as clk:
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        ops.check_status(dev, "bench warm-up")
+        barrier(world)
+        torch.cuda.synchronize(dev)
         t0.record(stream)
         for _ in range(args.steps):
             graph.replay()
@@ -949,7 +965,7 @@ def run_mserve(args, world, rank, local):
                                        "note": "rank 0's share; each phase of all layers replayed alone as a CUDA "
                                                "graph after the timed region; the attention then reads its rows "
                                                "from L2"},
-            "serial_ms_per_step": serial_ms_step, "chunks": args.chunks,
+            "serial_ms_per_step": serial_ms_step, "chunks": args.chunks, "gather_ctas": args.gather_ctas or "default",
             "append_turn": turn,
             "pcie_peak_gbs": peaks,
             "pcie_peak_gbs_all_ranks": peaks_all,

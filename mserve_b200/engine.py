@@ -114,6 +114,9 @@ class OffloadKV:
         self._stage = torch.empty(6 * batch, dtype=torch.int32).pin_memory()
         self._pt_stage = torch.empty(batch, self.max_pages, dtype=torch.int32).pin_memory()
         self._stage_ev: Optional[torch.cuda.Event] = None
+        # CTAs of every move that reads host memory (the gathers and the window copies); 0: the
+        # library's default bound
+        self.host_link_ctas = 0
 
     # ------------------------------------------------------------------ append
     def reserve(self, n_new: Sequence[int]) -> None:
@@ -281,7 +284,7 @@ class OffloadKV:
         src = ops.strided_rows(self.host_k[layer], self.host_v[layer], len_=self.lens,
                                ring_start=self.ring_start, ring_cap=self.C, device=self.device)
         ops.gather(src, idx.view(self.B, self.Hkv, -1), bufs.k_sel, bufs.v_sel, batch=self.B,
-                   counts=counts.view(self.B, self.Hkv))
+                   counts=counts.view(self.B, self.Hkv), max_ctas=self.host_link_ctas)
         return bufs.k_sel, bufs.v_sel
 
     def attend(self, q: torch.Tensor, counts: torch.Tensor, bufs: Optional[DecodeBuffers] = None) -> torch.Tensor:
@@ -320,7 +323,7 @@ class OffloadKV:
         n0, kp, w = self.split[0], self.split[1], self.split[2]
         dst = ops.strided_rows(k_sel, v_sel, tok0=kp, device=self.device)
         ops.copy_rows(self._host_rows(layer, 0, self.B, tok0=n0), dst, batch=self.B, num_tokens=self.recent,
-                      counts=w, device=self.device)
+                      counts=w, device=self.device, max_ctas=self.host_link_ctas)
 
     def _chunk_ops(self, layer: int, q: torch.Tensor, b0: int, b1: int, bufs: DecodeBuffers, T: int,
                    sel_rows=None, window_done: bool = False):
@@ -347,7 +350,7 @@ class OffloadKV:
 
         def gather():
             ops.gather(self._host_rows(layer, b0, b1), idx.view(nb, Hkv, -1), k_sel, v_sel, batch=nb,
-                       counts=gcounts.view(nb, -1))
+                       counts=gcounts.view(nb, -1), max_ctas=self.host_link_ctas)
 
         def attend(out):
             ops.sparse_attention(q[b0:b1].unsqueeze(2), k_sel, v_sel, counts=counts.view(nb, Hkv), out=out[b0:b1])
