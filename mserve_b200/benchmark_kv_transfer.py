@@ -15,7 +15,10 @@ are checked against each other bit for bit, and times come from CUDA events.
 tokens.  For each point it reports the gather GB/s (selected token rows = all heads of a
 token, 2 KiB bf16 / 1 KiB fp8, host->HBM) and the write-back GB/s (the same number of rows,
 HBM->host ring positions), each against the pinned cudaMemcpyAsync peak of this GPU's host
-link in the same direction.  Under torchrun every rank runs the sweep on its own GPU and host
+link in the same direction: one transfer alone (replayed as a CUDA graph: its launch and ramp
+on the device included, the host time of the Python call not; that call's own rate is
+gather_api_call_gbs), a train of 8 back to back (as a decode loop issues them), and, as the
+reference for that transfer size, a pinned cudaMemcpyAsync of the same byte count.  Under torchrun every rank runs the sweep on its own GPU and host
 link; rank 0 prints per-point aggregate GB/s (sum over ranks, time = max over ranks) against the
 aggregate memcpy peak (every rank's peak measured at the same time, summed).
 
@@ -67,6 +70,25 @@ def structured_indices(n_tokens: int, n_sel: int, run: int, gen: torch.Generator
     starts = torch.randperm(n_tokens // run, generator=gen)[:n_runs].sort().values * run
     idx = (starts[:, None] + torch.arange(run)[None, :]).reshape(-1)
     return idx[:n_sel].sort().values
+
+
+TRAIN = 8   # gathers per back-to-back train
+
+
+def graph_timed(fn, reps: int) -> float:
+    """Median milliseconds of fn() captured as a CUDA graph and replayed alone (the device time of
+    its kernels, without the host time of the Python call)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    ms = timed(g.replay, reps)
+    del g
+    return ms
 
 
 def timed(fn, reps: int, warmup: int = 2) -> float:
@@ -155,6 +177,8 @@ def run_sweep(args, device, world: int, rank: int):
              "per_rank_d2h": own["d2h"], "ranks": world}
     gen = torch.Generator().manual_seed(4)
     lines = []
+    mc_host = torch.empty(T * H * D * 2 // 2, dtype=torch.uint8).pin_memory()   # the largest point (50%, bf16)
+    mc_dev = torch.empty_like(mc_host, device=device)
     for dtype in (torch.bfloat16, torch.float8_e4m3fn):
         es = torch.empty((), dtype=dtype).element_size()
         host = ops.host_empty((T, H, D), dtype)
@@ -169,7 +193,12 @@ def run_sweep(args, device, world: int, rank: int):
                 n_sel = idx.numel()
                 dev_rows = torch.empty(1, 1, n_sel, H * D, dtype=dtype, device=device)
                 src = ops.strided_rows(host_rows, None, device=device)
-                ms_g = timed(lambda: ops.gather(src, idx, dev_rows, None, batch=1), args.iterations)
+                ms_api = timed(lambda: ops.gather(src, idx, dev_rows, None, batch=1), args.iterations)
+                ms_g = graph_timed(lambda: ops.gather(src, idx, dev_rows, None, batch=1), args.iterations)
+                # a train of TRAIN gathers back to back (as a decode loop issues them): the launch
+                # and ramp of one transfer overlap the tail of the previous one
+                ms_gt = timed(lambda: [ops.gather(src, idx, dev_rows, None, batch=1) for _ in range(TRAIN)],
+                              max(2, args.iterations // 2)) / TRAIN
                 # correctness: bit-exact against the host rows
                 got = dev_rows.view(torch.uint8).cpu() if es == 1 else dev_rows.view(torch.int16).cpu()
                 ref = host_rows[0, 0][idx.cpu().long()]
@@ -179,18 +208,30 @@ def run_sweep(args, device, world: int, rank: int):
                 ring = torch.tensor([int(T // 3)], dtype=torch.int32, device=device)
                 dst = ops.strided_rows(host_rows, None, len_scalar=T, ring_start=ring, ring_cap=T, device=device)
                 srcw = ops.strided_rows(dev_rows, None, device=device)
-                ms_w = timed(lambda: ops.copy_rows(srcw, dst, batch=1, num_tokens=n_sel, device=device),
-                             args.iterations)
+                ms_w = graph_timed(lambda: ops.copy_rows(srcw, dst, batch=1, num_tokens=n_sel, device=device),
+                                   args.iterations)
+                ms_wt = timed(lambda: [ops.copy_rows(srcw, dst, batch=1, num_tokens=n_sel, device=device)
+                                       for _ in range(TRAIN)], max(2, args.iterations // 2)) / TRAIN
                 ops.check_status(device, "transfer sweep")
                 nbytes = n_sel * row_bytes
-                ms_g = _max(ms_g, world)
-                ms_w = _max(ms_w, world)
+                # a pinned cudaMemcpyAsync of the same byte count: what the copy engine reaches at
+                # this transfer size (contiguous, so an upper reference for a scattered gather)
+                ms_mc = timed(lambda: mc_dev[:nbytes].copy_(mc_host[:nbytes], non_blocking=True), args.iterations)
+                ms_g, ms_gt, ms_w, ms_wt, ms_mc, ms_api = (_max(x, world) for x in (ms_g, ms_gt, ms_w, ms_wt, ms_mc,
+                                                                                   ms_api))
                 agg = nbytes * world            # every rank moved nbytes; time = the slowest rank
                 line = {"mode": "sweep", "dtype": str(dtype).replace("torch.", ""), "tokens": T, "heads": H,
                         "head_dim": D, "density": density, "structure": "random" if run == 1 else f"runs{run}",
                         "rows": n_sel, "row_bytes": row_bytes, "n_gpus": world,
                         "gather_gbs": agg / (ms_g * 1e-3) / 1e9, "gather_frac_h2d_peak": agg / (ms_g * 1e-3) / 1e9 / peaks["h2d"],
                         "writeback_gbs": agg / (ms_w * 1e-3) / 1e9, "writeback_frac_d2h_peak": agg / (ms_w * 1e-3) / 1e9 / peaks["d2h"],
+                        "gather_api_call_gbs": agg / (ms_api * 1e-3) / 1e9,
+                        "gather_train_gbs": agg / (ms_gt * 1e-3) / 1e9,
+                        "gather_train_frac_h2d_peak": agg / (ms_gt * 1e-3) / 1e9 / peaks["h2d"],
+                        "writeback_train_gbs": agg / (ms_wt * 1e-3) / 1e9,
+                        "writeback_train_frac_d2h_peak": agg / (ms_wt * 1e-3) / 1e9 / peaks["d2h"],
+                        "memcpy_same_bytes_gbs": agg / (ms_mc * 1e-3) / 1e9,
+                        "gather_frac_same_bytes_memcpy": ms_mc / ms_g,
                         "gather_ms": ms_g, "writeback_ms": ms_w, "memcpy_peak_gbs": peaks, "bit_exact": True}
                 lines.append(line)
                 if rank == 0:
