@@ -754,6 +754,7 @@ def run_mserve(args, world, rank, local):
     peaks = pcie_peaks(dev, world)
     peaks_all = {"h2d_sum": sum_over_ranks(peaks["h2d"], world), "d2h_sum": sum_over_ranks(peaks["d2h"], world),
                  "h2d_min_rank": min_over_ranks(peaks["h2d"], world),
+                 "h2d_per_rank": gather_objects(round(peaks["h2d"], 2), world),
                  "note": f"per rank the median of {PEAK_REPS} pinned 1 GiB cudaMemcpyAsync copies, every copy "
                          "started after a barrier so all ranks copy at once; summed over ranks"}
     gb_layer = gathered_bytes(eng)
@@ -815,6 +816,7 @@ def run_mserve(args, world, rank, local):
     serial_ms_step = L * (sel_ms + gat_ms + att_ms)
     ops.check_status(dev, "bench phase timing")
     gat_ms_max = max_over_ranks(gat_ms, world)
+    gat_ms_ranks = gather_objects(round(gat_ms, 5), world)
 
     # end to end through the public API: q from pinned host each step, outputs back to host
     e2e = None
@@ -961,6 +963,7 @@ def run_mserve(args, world, rank, local):
             "parity": parity,
             "roofline": roofline, "roofline_select": roofline_select,
             "breakdown_ms_per_layer": {"score_topk": sel_ms, "gather": gat_ms, "gather_max_over_ranks": gat_ms_max,
+                                       "gather_per_rank": gat_ms_ranks,
                                        "attention": att_ms,
                                        "note": "rank 0's share; each phase of all layers replayed alone as a CUDA "
                                                "graph after the timed region; the attention then reads its rows "
@@ -970,6 +973,8 @@ def run_mserve(args, world, rank, local):
             "pcie_peak_gbs": peaks,
             "pcie_peak_gbs_all_ranks": peaks_all,
             "gather_frac_of_concurrent_h2d_peak_whole_step": value / peaks_all["h2d_sum"],
+            # equal shares finish with the slowest rank: its concurrent link rate x N bounds the job
+            "gather_frac_of_slowest_rank_peak_x_n": value / (peaks_all["h2d_min_rank"] * world),
             "host_placement": {"numa_node": numa_node, "local_cpus": len(eng.host_cpus),
                                "note": "host store allocated on the GPU's local CPUs (0: placement left to the system)"},
             "shared_selection": shared,
