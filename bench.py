@@ -266,7 +266,7 @@ def measured_peaks():
 NCU_TRAFFIC = {
     "gather": {"link_bytes": (1048576 + 65536) * 32,
                "source": "profiles/gather_decode_qwen7b.txt (move_rows_kernel<16>, ncu --set full)"},
-    "select": {"dram_bytes": 138077440 + 2138880,
+    "select": {"dram_bytes": 134962432 + 5281792 + 2126592,
                "source": "profiles/select_decode_qwen7b.txt (score_stream_kernel + topk_smem_kernel<1>, ncu --set full)"},
 }
 
