@@ -96,6 +96,8 @@ def parse():
     ap.add_argument("--no-decode-loop", action="store_true")
     ap.add_argument("--no-exchange", action="store_true", help="skip the shared-selection exchange timing")
     ap.add_argument("--no-parity", action="store_true", help="skip the per-rank check against the unsharded layer")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the 32B-shape decode (4 layers) and the transfer-sweep points of the line")
     ap.add_argument("--chunks", type=int, default=4, help="sequence chunks pipelined per layer")
     ap.add_argument("--gather-ctas", type=int, default=0,
                     help="CTAs of each host-memory gather (0: the library's default bound)")
@@ -729,6 +731,79 @@ def shared_selection_timing(wl, plan, eng, q, world, dev, L_time, reps=4):
     return res
 
 
+def extra_qwen32b(world, rank, dev, steps, warmup, chunks, layers=4):
+    """The Qwen2.5-VL-32B decode shape (16 x 32768 tokens, 40/8 heads, top-4096 + last 256), its
+    KV heads split over the ranks like the main workload, `layers` of its 64 layers: whole-job
+    GB/s and step ms (max over ranks) of the captured step."""
+    from mserve_b200 import ops, parallel
+    wl = dict(WORKLOADS["qwen32b"][0], layers=layers)
+    plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank)
+    eng, q = build_engine(wl, plan, dev)
+    out = torch.empty((wl["layers"],) + tuple(eng.buffers().out.shape), dtype=eng.dtype, device=dev)
+    g = eng.capture_decode_step(q, out, chunks=chunks)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ops.check_status(dev, "32B-shape decode")
+    t = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    total = sum_over_ranks(gathered_bytes(eng) * wl["layers"] * steps, world)
+    del g, eng, q, out
+    torch.cuda.empty_cache()
+    return {"value": total / t / 1e9, "unit": "GB/s", "ms_per_step": t / steps * 1e3, "layers": wl["layers"],
+            "of_layers": 64, "steps": steps,
+            "shard": {"kv_heads_per_rank": plan.h1 - plan.h0, "sequences_per_rank": plan.b1 - plan.b0},
+            "workload": WORKLOADS["qwen32b"][1] + f" ({layers} of its 64 layers)"}
+
+
+def extra_transfer_points(world, dev, peaks):
+    """Points of the transfer sweep (one token-major layer [131072, 8, 128], whole-token rows,
+    uniform-random selections, seed 4) on every rank at once: gather host->HBM and write-back
+    HBM->host, each transfer replayed as a CUDA graph; GB/s over all ranks (time = slowest rank)
+    against the ranks' concurrent memcpy peaks."""
+    from mserve_b200 import ops
+    from mserve_b200.benchmark_kv_transfer import graph_timed, structured_indices
+    T, H, D = 131072, 8, 128
+    gen = torch.Generator().manual_seed(4)
+    pts = []
+    for dtype in (torch.bfloat16, torch.float8_e4m3fn):
+        es = torch.empty((), dtype=dtype).element_size()
+        host = ops.host_empty((T, H, D), dtype)
+        host.copy_(torch.randn(T, H, D, generator=gen).to(dtype))
+        rows = host.view(1, 1, T, H * D)
+        src = ops.strided_rows(rows, None, device=dev)
+        for density in (0.05, 0.50):
+            idx = structured_indices(T, int(T * density), 1, gen).to(torch.int32).to(dev)
+            n = idx.numel()
+            dst = torch.empty(1, 1, n, H * D, dtype=dtype, device=dev)
+            barrier(world)
+            ms_g = graph_timed(lambda: ops.gather(src, idx, dst, None, batch=1), 10)
+            ok = torch.equal(dst[0, 0].cpu().view(torch.uint8), rows[0, 0][idx.cpu().long()].view(torch.uint8))
+            ring = torch.tensor([T // 3], dtype=torch.int32, device=dev)
+            wdst = ops.strided_rows(rows, None, len_scalar=T, ring_start=ring, ring_cap=T, device=dev)
+            wsrc = ops.strided_rows(dst, None, device=dev)
+            barrier(world)
+            ms_w = graph_timed(lambda: ops.copy_rows(wsrc, wdst, batch=1, num_tokens=n, device=dev), 10)
+            ops.check_status(dev, "transfer points")
+            nbytes = n * H * D * es
+            tg, tw = max_over_ranks(ms_g, world), max_over_ranks(ms_w, world)
+            g_all, w_all = nbytes * world / (tg * 1e-3) / 1e9, nbytes * world / (tw * 1e-3) / 1e9
+            pts.append({"dtype": str(dtype).replace("torch.", ""), "density": density, "rows": n,
+                        "gather_gbs": g_all, "gather_frac_concurrent_h2d": g_all / peaks["h2d_sum"],
+                        "writeback_gbs": w_all, "writeback_frac_concurrent_d2h": w_all / peaks["d2h_sum"],
+                        "bit_exact_ranks": int(sum_over_ranks(float(ok), world))})
+        del host
+    return {"layer": f"[{T} tokens, {H} KV heads, {D}] token-major, uniform-random selections, every rank at once",
+            "points": pts}
+
+
 def run_mserve(args, world, rank, local):
     from mserve_b200 import _lib, ops, parallel, topology
     dev = torch.device("cuda", local)
@@ -861,6 +936,12 @@ def run_mserve(args, world, rank, local):
             if own_group:
                 dist.destroy_process_group()
 
+    # The 32B shape and transfer-sweep points on the same ranks (configurations 3 and 5).
+    extra = None
+    if not args.no_extra:
+        extra = {"qwen32b_decode": extra_qwen32b(world, rank, dev, args.steps, args.warmup, args.chunks),
+                 "transfer": extra_transfer_points(world, dev, peaks_all)}
+
     # CPU baseline: the C restatement on this host's cores, rank 0 at N=1 only
     cpu = None
     fixed_shape = "lens_uniform" not in wl and "top_k_ratio" not in wl   # what the C port restates
@@ -978,6 +1059,7 @@ def run_mserve(args, world, rank, local):
             "host_placement": {"numa_node": numa_node, "local_cpus": len(eng.host_cpus),
                                "note": "host store allocated on the GPU's local CPUs (0: placement left to the system)"},
             "shared_selection": shared,
+            "extra_workloads": extra,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "decode_loop": loop,
             "clocks": clk.summary(),
         }
