@@ -5,13 +5,19 @@
 // (no repeat_kv): all G query heads (times q_len query rows) of a KV head are served by one
 // pass over that head's selected rows, so every gathered byte is read once from HBM.
 //
-// Split-sequence ("flash-decoding") schedule on the tensor cores, fast path (16-bit, D in
-// {64,128}, G*q_len <= 16, 16-byte aligned rows): CTA (segment, split) owns kAtTile = 128
-// selected rows, 32 per warp; see attn_mma_kernel.  The splits' (m, l, O) partials are merged
-// by a second kernel, one block per (segment, query row).
+// Fast path (16-bit, D in {64,128}, G*q_len <= 16, 16-byte aligned rows and strides), on the
+// tensor cores (mma.sync m16n8k16, fp32 accumulate):
+//  * selections of up to 8 x 4096 rows: one streaming kernel, the CTAs of a segment forming a
+//    thread-block cluster that merges through distributed shared memory (attn_cluster_kernel;
+//    TMA tile loads, no workspace);
+//  * wider selections: split-sequence ("flash-decoding") schedule, CTA (segment, split) owns
+//    kAtTile = 128 rows (attn_mma_kernel), the splits' (m, l, O) partials in a workspace merged
+//    by a second kernel, one block per (segment, query row).
 // Other shapes use a one-warp-per-output-row kernel with an online softmax.
+#include <cuda.h>   // CUtensorMap and its enums; the encoder is reached through the runtime
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 
@@ -41,6 +47,7 @@ struct AttnDev {
   uint32_t* status;
   float scale;
   int32_t batch, q_heads, kv_heads, head_dim, q_len, num_sel, splits, nr, dtype;
+  int32_t rps;             // streaming cluster path: selected rows per CTA (splits = CTAs per cluster)
 };
 
 template <typename T> __device__ __forceinline__ float to_f(T x);
@@ -367,6 +374,430 @@ __global__ void __launch_bounds__(D) attn_merge_kernel(const AttnDev a) {
   op[d] = from_f<T>(L > 0.f ? o / L : 0.f);
 }
 
+// ---- streaming cluster path ------------------------------------------------------------
+// One kernel per call, no workspace.  The CTAs of a segment (a (sequence, KV head) pair) form
+// a thread-block cluster of cs <= 8; CTA c owns the selected rows [c*rps, (c+1)*rps), where cs
+// and rps depend only on the selection width (so a segment is split the same way whatever the
+// batch, the chunking or the head sharding of the call, and outputs are bit-identical across
+// them).  Inside a CTA every warp streams its own 16-row blocks (blocks warp, warp+4, ...)
+// through a private ring of kAcStages stages: one elected lane issues the block's K and V as
+// tiled TMA loads (3-D tensor maps [segment][row][dim], 128-byte boxes with the 128-byte
+// swizzle, so ldmatrix reads are bank-conflict free without padding) that complete on the
+// stage's mbarrier, and refills the stage as soon as the warp has read it.  Rows past the
+// selection width arrive zero-filled by the TMA unit; V rows between the segment's count and
+// the width are zeroed in shared memory, so the masked (P = 0) columns of P·V stay finite.
+// Each warp keeps an online softmax (running max, normaliser, O) in registers; the four warps
+// merge in shared memory into the CTA's partial, and the cluster merges its CTAs' partials
+// through distributed shared memory and writes the output.  Every mbarrier wait is bounded:
+// past the limit the warp sets MSKV_STATUS_TIMEOUT, waits (bounded) for its other loads in
+// flight, drops its rows and still takes every barrier, so the CTA and the cluster finish.
+constexpr int kAcWarps = 4;
+constexpr int kAcStages = 3;          // per warp
+constexpr int kAcBlock = 16;          // selected rows per block (one k-step of P·V)
+constexpr int kAcMaxCluster = 8;      // portable cluster size
+constexpr int kAcRowsPerCta = 256;    // split target: cs = ceil(width / 256), at most 8
+constexpr int kAcMaxWidth = kAcMaxCluster * 4096;   // wider selections take the split path
+constexpr int kAcWaitIters = 1 << 22;
+
+template <int D>
+struct AcShape {
+  static constexpr int HALVES = D / 64;                    // 128-byte column boxes per row
+  static constexpr int HB = kAcBlock * 128;                // one box: 16 rows x 128 bytes
+  static constexpr int KB = HALVES * HB;                   // K (or V) bytes of a block
+  static constexpr int SB = 2 * KB;                        // stage: K block then V block
+  static constexpr int ROWP = D * 2 + 16;                  // padded query row (bytes)
+  static constexpr int SMEM = kAcWarps * kAcStages * SB + 16 * ROWP + 1024;   // + alignment slack
+};
+
+__device__ __forceinline__ bool ac_wait(uint32_t bar, uint32_t parity) {
+  for (int it = 0; it < kAcWaitIters; ++it) {
+    uint32_t done;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void ac_tma_load(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+               ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar) : "memory");
+}
+
+// 2^x by the SFU (ex2.approx.ftz: relative error about 2^-22; 2^-inf = 0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(remote)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// Byte offset of 16-byte chunk c (of a row of D/8 chunks) of block row `row` in a block stored
+// as 128-byte-swizzled boxes of 16 rows x 128 bytes (chunk (c & 7) of box (c >> 3) sits at
+// position (c & 7) ^ (row & 7) of its 128-byte line).
+__device__ __forceinline__ int ac_swz(int row, int c) {
+  return (c >> 3) * (kAcBlock * 128) + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+}
+
+template <bool BF16, int D>
+__global__ void __launch_bounds__(kAcWarps * 32, 2)
+    attn_cluster_kernel(const AttnDev a, const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv) {
+  allow_dependents();
+  using SH = AcShape<D>;
+  constexpr int KS = D / 16;            // k-steps of Q·Kᵀ
+  constexpr int NT = D / 8;             // n-tiles of P·V
+  constexpr int OS = D + 8;             // padded row of a warp's fp32 partial
+  static_assert(16 * OS * 4 <= 2 * SH::SB, "a warp's partial must fit in two of its stages");
+  static_assert(16 * D * 4 <= SH::SB, "the CTA partial must fit in one stage");
+  extern __shared__ uint8_t ac_raw[];
+  __shared__ __align__(8) uint64_t bars[kAcWarps][kAcStages];
+  __shared__ float s_m[kAcWarps][16], s_l[kAcWarps][16];
+  __shared__ float c_m[16], c_l[16];
+  uint8_t* smem = ac_raw + ((1024u - (smem_u32(ac_raw) & 1023u)) & 1023u);   // 1024-aligned (swizzle atom)
+  uint8_t* sQ = smem + kAcWarps * kAcStages * SH::SB;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tig = lane & 3;
+  const int cs = a.splits;
+  const int seg = blockIdx.x / cs;
+  uint32_t crank;
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+  const int b = seg / a.kv_heads;
+  const int hk = seg - b * a.kv_heads;
+  const int G = a.q_heads / a.kv_heads;
+  const int nr = a.nr;
+  int count = a.counts ? a.counts[seg] : a.num_sel;
+  if (count > a.num_sel) count = a.num_sel;
+  if (count < 0) count = 0;
+  const int rb = (int)crank * a.rps;
+  const int re = min(count, rb + a.rps);
+  const int nblk = re > rb ? (re - rb + kAcBlock - 1) / kAcBlock : 0;
+  const int nw = nblk > warp ? (nblk - warp + kAcWarps - 1) / kAcWarps : 0;   // this warp's blocks
+
+  uint8_t* wst = smem + warp * kAcStages * SH::SB;     // this warp's stages
+  const uint32_t bar0 = smem_u32(&bars[warp][0]);     // stage s's mbarrier: bar0 + 8 s
+  auto issue = [&](int i) {                            // lane 0: block i of this warp into its stage
+    const int s = i % kAcStages;
+    const int y = rb + (warp + kAcWarps * i) * kAcBlock;
+    const uint32_t dk = smem_u32(wst + s * SH::SB), dv = dk + SH::KB;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar0 + 8 * s), "r"(SH::SB) : "memory");
+#pragma unroll
+    for (int h = 0; h < SH::HALVES; ++h) {
+      ac_tma_load(dk + h * SH::HB, &tk, h * 64, y, seg, bar0 + 8 * s);
+      ac_tma_load(dv + h * SH::HB, &tv, h * 64, y, seg, bar0 + 8 * s);
+    }
+  };
+  // query rows (zero beyond nr) in 16-byte chunks, requested before the block loads so they do
+  // not queue behind them
+  constexpr int CPR = D * 2 / 16;
+  constexpr int QPT = 16 * CPR / (kAcWarps * 32);      // chunks per thread
+  uint4 qv[QPT];
+#pragma unroll
+  for (int k = 0; k < QPT; ++k) {
+    const int x = tid + k * kAcWarps * 32;
+    const int r = x / CPR, c = x - r * CPR;
+    qv[k] = make_uint4(0, 0, 0, 0);
+    if (r < nr) {
+      const int gq = r / a.q_len, i = r - gq * a.q_len;
+      qv[k] = *reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_sb + (int64_t)(hk * G + gq) * a.q_sh +
+                                              (int64_t)i * a.q_sq + c * 16);
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kAcStages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < nw && i < kAcStages; ++i) issue(i);
+  }
+#pragma unroll
+  for (int k = 0; k < QPT; ++k) {
+    const int x = tid + k * kAcWarps * 32;
+    const int r = x / CPR, c = x - r * CPR;
+    *reinterpret_cast<uint4*>(sQ + r * SH::ROWP + c * 16) = qv[k];
+  }
+  __syncthreads();
+  uint32_t qa[KS][4];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk) {
+    const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int col = kk * 16 + 8 * (lane >> 4);
+    ldsm_x4(qa[kk], sQ + row * SH::ROWP + col * 2);
+  }
+
+  const float sl2 = a.scale * 1.4426950408889634f;     // exponent base 2: exp(x) = 2^(x log2 e)
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  float oacc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) oacc[n][e] = 0.f;
+  bool ok = true;
+  const bool hi_rows = nr > 8;                         // query rows 8..15 exist
+  for (int i = 0; i < nw; ++i) {
+    const int s = i % kAcStages;
+    uint32_t done = 0;
+    if (lane == 0) done = ac_wait(bar0 + 8 * s, (uint32_t)(i / kAcStages) & 1u);
+    done = __shfl_sync(0xffffffffu, done, 0);
+    if (!done) {                                       // record it, let the other loads land, stop
+      if (lane == 0) {
+        if (a.status) atomicOr(a.status, MSKV_STATUS_TIMEOUT);
+        for (int j = i; j < nw && j < i + kAcStages; ++j)
+          ac_wait(bar0 + 8 * (j % kAcStages), (uint32_t)(j / kAcStages) & 1u);
+      }
+      __syncwarp();
+      ok = false;
+      break;
+    }
+    uint8_t* sK = wst + s * SH::SB;
+    uint8_t* sV = sK + SH::KB;
+    const int y0 = rb + (warp + kAcWarps * i) * kAcBlock;
+    const int vrows = min(kAcBlock, re - y0);
+    if (vrows < kAcBlock) {                            // rows past the count: zero V
+      for (int x = lane; x < (kAcBlock - vrows) * 8 * SH::HALVES; x += 32) {
+        const int r = vrows + x / (8 * SH::HALVES), c = x % (8 * SH::HALVES);
+        *reinterpret_cast<uint4*>(sV + ac_swz(r, c)) = make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+    }
+    // S = Q·Kᵀ over the block's 16 rows: n-tile j covers rows 8j .. 8j+7; even and odd k-steps
+    // accumulate separately (two short dependency chains per n-tile instead of one long one)
+    float sacc[2][4], sodd[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sacc[j][e] = sodd[j][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KS; kk += 2) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t kb[4];
+        const int row = 8 * j + (lane & 7);
+        ldsm_x4(kb, sK + ac_swz(row, 2 * kk + (lane >> 3)));
+        mma16816<BF16>(sacc[j], qa[kk], kb[0], kb[1]);
+        mma16816<BF16>(sodd[j], qa[kk + 1], kb[2], kb[3]);
+      }
+    }
+    // online softmax in base 2: rows g (e < 2) and g + 8 (e >= 2); the four lanes of a group
+    // share a row.  With at most 8 query rows (hi_rows false) rows g + 8 are padding: their
+    // probabilities are set to 0 and nothing else is computed for them.
+    float bm_lo = -INFINITY, bm_hi = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = 8 * j + 2 * tig + (e & 1);
+        const float v = col < vrows ? (sacc[j][e] + sodd[j][e]) * sl2 : -INFINITY;
+        sacc[j][e] = v;
+        if (e < 2) bm_lo = fmaxf(bm_lo, v);
+        else bm_hi = fmaxf(bm_hi, v);
+      }
+    }
+    bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, 1));
+    bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, 2));
+    if (hi_rows) {
+      bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 1));
+      bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 2));
+    }
+    const float mn_lo = fmaxf(m_lo, bm_lo);            // finite: the block has a valid row
+    const float mn_hi = hi_rows ? fmaxf(m_hi, bm_hi) : m_hi;
+    const bool moved = __any_sync(0xffffffffu, mn_lo != m_lo || mn_hi != m_hi);
+    float p_lo = 0.f, p_hi = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sacc[j][e] = ex2(sacc[j][e] - mn_lo);          // masked: 2^-inf = 0
+        p_lo += sacc[j][e];
+        if (hi_rows) {
+          sacc[j][e + 2] = ex2(sacc[j][e + 2] - mn_hi);
+          p_hi += sacc[j][e + 2];
+        } else {
+          sacc[j][e + 2] = 0.f;
+        }
+      }
+    }
+    if (moved) {                                       // rescale what was summed under the old maxima
+      const float c_lo = ex2(m_lo - mn_lo);             // 0 while nothing was seen, 1 if unchanged
+      const float c_hi = hi_rows ? ex2(m_hi - mn_hi) : 1.f;
+      l_lo *= c_lo;
+      l_hi *= c_hi;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        oacc[n][0] *= c_lo;
+        oacc[n][1] *= c_lo;
+        if (hi_rows) {
+          oacc[n][2] *= c_hi;
+          oacc[n][3] *= c_hi;
+        }
+      }
+      m_lo = mn_lo;
+      m_hi = mn_hi;
+    }
+    l_lo += p_lo;
+    l_hi += p_hi;
+    // O += P·V: P as the A fragment of one 16-row k-step, V through ldmatrix.trans
+    uint32_t pa[4];
+    pa[0] = pack2<BF16>(sacc[0][0], sacc[0][1]);
+    pa[1] = pack2<BF16>(sacc[0][2], sacc[0][3]);
+    pa[2] = pack2<BF16>(sacc[1][0], sacc[1][1]);
+    pa[3] = pack2<BF16>(sacc[1][2], sacc[1][3]);
+#pragma unroll
+    for (int n = 0; n < NT; n += 2) {
+      uint32_t vb[4];
+      const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+      ldsm_x4_t(vb, sV + ac_swz(row, n + (lane >> 4)));
+      mma16816<BF16>(oacc[n], pa, vb[0], vb[1]);
+      mma16816<BF16>(oacc[n + 1], pa, vb[2], vb[3]);
+    }
+    __syncwarp();                                      // every lane has read the stage
+    if (lane == 0 && i + kAcStages < nw) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // reads/zeroes before the refill
+      issue(i + kAcStages);
+    }
+  }
+  if (!ok) {
+    m_lo = m_hi = -INFINITY;
+    l_lo = l_hi = 0.f;
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) oacc[n][e] = 0.f;
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, o);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, o);
+  }
+  // the warp's partial -> its first two stages (all its loads have landed)
+  float* so = reinterpret_cast<float*>(wst);
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int col = n * 8 + 2 * tig;
+    *reinterpret_cast<float2*>(so + g * OS + col) = make_float2(oacc[n][0], oacc[n][1]);
+    *reinterpret_cast<float2*>(so + (g + 8) * OS + col) = make_float2(oacc[n][2], oacc[n][3]);
+  }
+  if (tig == 0) {
+    s_m[warp][g] = m_lo;
+    s_m[warp][g + 8] = m_hi;
+    s_l[warp][g] = l_lo;
+    s_l[warp][g + 8] = l_hi;
+  }
+  __syncthreads();
+  // four warps -> the CTA's partial (warp 0's third stage, which no warp uses any more): one pass,
+  // four output dims per thread, every input requested before the first is used
+  constexpr int D4 = D / 4;
+  float* co = reinterpret_cast<float*>(smem + 2 * SH::SB);
+  for (int x = tid; x < nr * D4; x += kAcWarps * 32) {
+    const int r = x / D4, d = (x - r * D4) * 4;
+    float mw[kAcWarps], lw[kAcWarps];
+    float4 ow[kAcWarps];
+#pragma unroll
+    for (int w = 0; w < kAcWarps; ++w) {
+      mw[w] = s_m[w][r];
+      lw[w] = s_l[w][r];
+      ow[w] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(smem + w * kAcStages * SH::SB) + r * OS + d);
+    }
+    float M = mw[0];
+#pragma unroll
+    for (int w = 1; w < kAcWarps; ++w) M = fmaxf(M, mw[w]);
+    float L = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kAcWarps; ++w) {
+      const float f = mw[w] == -INFINITY ? 0.f : exp2f(mw[w] - M);
+      L += lw[w] * f;
+      o.x += ow[w].x * f;
+      o.y += ow[w].y * f;
+      o.z += ow[w].z * f;
+      o.w += ow[w].w * f;
+    }
+    *reinterpret_cast<float4*>(co + r * D + d) = o;
+    if (d == 0) {
+      c_m[r] = M;
+      c_l[r] = L;
+    }
+  }
+  if (cs > 1) cluster_sync_all();
+  else __syncthreads();
+  // the cluster's CTAs -> the output.  Query row r is finished by CTA r mod cs, four dims per
+  // thread; the D/4 lanes that share a row fetch the cs peers' maxima and normalisers once
+  // (lane q of the group from peer q) and pass them on with shuffles, and every peer's four dims
+  // are requested before the first is used.
+  static_assert(D4 >= kAcMaxCluster && 32 % D4 == 0, "a row's lanes must cover the cluster");
+  const uint32_t co_a = smem_u32(co), cm_a = smem_u32(c_m), cl_a = smem_u32(c_l);
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  const int my_rows = nr > (int)crank ? (nr - (int)crank + cs - 1) / cs : 0;
+  const int gbase = lane & ~(D4 - 1), li = lane & (D4 - 1);     // this lane's row group in the warp
+  for (int y0 = warp * 32; y0 < my_rows * D4; y0 += kAcWarps * 32) {   // warp-uniform trip count
+    const int y = y0 + lane;
+    const bool live = y < my_rows * D4;
+    const int r = live ? (int)crank + cs * (y / D4) : (int)crank;
+    const int d = (y % D4) * 4;
+    float mine_m = -INFINITY, mine_l = 0.f;
+    if (li < cs) {
+      mine_m = cs == 1 ? c_m[r] : ld_cluster_f32(cm_a + 4 * r, li);
+      mine_l = cs == 1 ? c_l[r] : ld_cluster_f32(cl_a + 4 * r, li);
+    }
+    float4 oq[kAcMaxCluster];
+#pragma unroll
+    for (int q = 0; q < kAcMaxCluster; ++q)
+      if (q < cs) oq[q] = cs == 1 ? *reinterpret_cast<const float4*>(co + r * D + d) : ld_cluster_f32x4(co_a + 4 * (r * D + d), q);
+    float mq[kAcMaxCluster], lq[kAcMaxCluster];
+#pragma unroll
+    for (int q = 0; q < kAcMaxCluster; ++q) {
+      mq[q] = __shfl_sync(0xffffffffu, mine_m, gbase + q);
+      lq[q] = __shfl_sync(0xffffffffu, mine_l, gbase + q);
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kAcMaxCluster; ++q)
+      if (q < cs) M = fmaxf(M, mq[q]);
+    float L = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < kAcMaxCluster; ++q) {
+      if (q < cs && mq[q] != -INFINITY) {
+        const float f = exp2f(mq[q] - M);
+        L += lq[q] * f;
+        o.x += oq[q].x * f;
+        o.y += oq[q].y * f;
+        o.z += oq[q].z * f;
+        o.w += oq[q].w * f;
+      }
+    }
+    if (live) {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      const int gq = r / a.q_len, i = r - gq * a.q_len;
+      T* op = reinterpret_cast<T*>(a.out + (int64_t)b * a.o_sb + (int64_t)(hk * G + gq) * a.o_sh + (int64_t)i * a.o_sq) + d;
+      op[0] = from_f<T>(o.x * inv);
+      op[1] = from_f<T>(o.y * inv);
+      op[2] = from_f<T>(o.z * inv);
+      op[3] = from_f<T>(o.w * inv);
+    }
+  }
+  if (cs > 1) cluster_sync_all();                      // no CTA leaves while a peer reads its partial
+}
+
 // Generic path: one warp per output row (b, hq, i); online softmax over the selected rows.
 template <typename T>
 __global__ void attn_generic_kernel(const AttnDev a) {
@@ -449,6 +880,89 @@ static int64_t splits_of(const mskv_attn_desc* d) {
   return d->num_selected > 0 ? (d->num_selected + kAtTile - 1) / kAtTile : 1;
 }
 
+// ---- streaming cluster path: tensor maps and the split -------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the library links only the
+// runtime); nullptr when the driver does not offer it.
+static EncodeTiledFn tensor_map_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// K or V rows as a 3-D tensor [segment][row][dim] of 16-bit elements with 16-row x 64-element
+// boxes and the 128-byte swizzle; rows past the width read as zeros.
+static bool encode_rows_map(CUtensorMap* m, const void* base, const mskv_attn_desc* d) {
+  const int64_t segs = (int64_t)d->batch * d->kv_heads;
+  const int64_t seg_stride = segs > 1 ? d->kv_stride_seg : (int64_t)d->num_selected * d->kv_stride_s;
+  const cuuint64_t dims[3] = {(cuuint64_t)d->head_dim, (cuuint64_t)d->num_selected, (cuuint64_t)segs};
+  const cuuint64_t strides[2] = {(cuuint64_t)d->kv_stride_s, (cuuint64_t)seg_stride};
+  const cuuint32_t box[3] = {64, (cuuint32_t)kAcBlock, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return tensor_map_encoder()(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct ClusterPlan {
+  bool use;
+  int cs;     // CTAs per segment (the cluster)
+  int rps;    // selected rows per CTA, a multiple of the 16-row block
+  CUtensorMap tk, tv;
+};
+
+// The split depends only on the selection width: cs = ceil(width / 256) CTAs (at most 8), each
+// with an equal multiple of 16 rows.  Selections wider than 8 x 4096 rows, empty ones, and rows
+// the TMA unit cannot address (strides not multiples of 16 bytes, checked by fast_path, or a
+// layout the tensor-map encoder refuses) take the split path.
+static void cluster_plan(const mskv_attn_desc* d, ClusterPlan* p) {
+  p->use = false;
+  if (!fast_path(d) || d->num_selected <= 0 || d->num_selected > kAcMaxWidth || d->batch <= 0) return;
+  if (d->kv_stride_s < d->head_dim * 2 || (d->batch * (int64_t)d->kv_heads > 1 && d->kv_stride_seg <= 0)) return;
+  if (!tensor_map_encoder() || !encode_rows_map(&p->tk, d->k, d) || !encode_rows_map(&p->tv, d->v, d)) return;
+  const int w = d->num_selected;
+  p->cs = std::min(kAcMaxCluster, std::max(1, (w + kAcRowsPerCta - 1) / kAcRowsPerCta));
+  const int blocks = (w + kAcBlock - 1) / kAcBlock;
+  p->rps = ((blocks + p->cs - 1) / p->cs) * kAcBlock;
+  p->use = true;
+}
+
+template <bool BF16, int D>
+static int launch_cluster(const AttnDev& a, const mskv_attn_desc* d, const ClusterPlan& p, cudaStream_t st) {
+  int rc;
+  const void* kern = (const void*)attn_cluster_kernel<BF16, D>;
+  rc = ensure_smem_limit(kern, AcShape<D>::SMEM, "mskv_sparse_attention");
+  if (rc) return rc;
+  const int64_t blocks = (int64_t)d->batch * d->kv_heads * p.cs;
+  if (blocks > 0x7fffffffLL) return fail(MSKV_ERR_RANGE, "mskv_sparse_attention: grid too large");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(kAcWarps * 32);
+  cfg.dynamicSmemBytes = AcShape<D>::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.cs > 1 ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_cluster_kernel<BF16, D>, a, p.tk, p.tv);
+  if (e != cudaSuccess) return cuda_status(e, "mskv_sparse_attention cluster launch");
+  return after_launch("mskv_sparse_attention");
+}
+
 }  // namespace mskv
 
 using namespace mskv;
@@ -456,6 +970,9 @@ using namespace mskv;
 extern "C" uint64_t mskv_attention_workspace_bytes(const mskv_attn_desc* d) {
   if (!d || d->kv_heads <= 0 || d->q_heads <= 0 || d->q_len <= 0 || d->batch < 0) return 0;
   if (!fast_path(d)) return 0;
+  ClusterPlan cp;
+  cluster_plan(d, &cp);
+  if (cp.use) return 0;
   const int64_t nr = (int64_t)(d->q_heads / d->kv_heads) * d->q_len;
   return (uint64_t)((int64_t)d->batch * d->kv_heads * splits_of(d) * nr * (d->head_dim + 2) * 4);
 }
@@ -482,6 +999,15 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
   a.head_dim = d->head_dim; a.q_len = d->q_len; a.num_sel = d->num_selected; a.dtype = d->dtype;
   a.nr = (d->q_heads / d->kv_heads) * d->q_len;
   cudaStream_t st = as_stream(stream);
+  ClusterPlan cp;
+  cluster_plan(d, &cp);
+  if (cp.use) {
+    a.splits = cp.cs;
+    a.rps = cp.rps;
+    const bool bf = d->dtype == MSKV_DT_BF16;
+    if (d->head_dim == 128) return bf ? launch_cluster<true, 128>(a, d, cp, st) : launch_cluster<false, 128>(a, d, cp, st);
+    return bf ? launch_cluster<true, 64>(a, d, cp, st) : launch_cluster<false, 64>(a, d, cp, st);
+  }
   if (fast_path(d)) {
     const uint64_t need = mskv_attention_workspace_bytes(d);
     if (!d->workspace || d->workspace_bytes < need)

@@ -5,10 +5,12 @@ unsafe (under an allocator lock, inside another library's memory pool, on a host
 allocation-free decode path).  The entry point uses a scratch array built into the library
 instead.  This test calls it through the C ABI (ctypes, no Python wrapper) and checks its
 output against the regular entry point, mskv_sparse_attention with a workspace, on calls in a
-row with different shapes -- the last one needing all but 2 KB of the built-in array, so its far
-end is written and read -- then checks that a shape one split too large for it is refused.
-Both entry points run the same kernels with the same split of the selected rows, so the
-outputs must be bit-identical.  The file is named to be collected last.
+row with different shapes, then checks that a shape one split too large for the array is
+refused.  Selections of up to 8 x 4096 rows run the streaming cluster kernel, which needs no
+scratch at all; wider ones run the split-sequence kernels, whose partials use the array -- the
+widest case here needs all but 2 KB of it, so its far end is written and read.  Both entry
+points run the same kernels with the same split of the selected rows, so the outputs must be
+bit-identical.  The file is named to be collected last.
 """
 import ctypes as C
 import math
@@ -59,7 +61,8 @@ def test_noalloc_attention_matches_workspace_entry_point(built_lib, seed):
     cases = [  # B, Hq, Hkv, Q, S, D, dtype, with counts
         (8, 28, 4, 1, 2176, 128, torch.bfloat16, False),   # the Qwen2.5-VL-7B decode selection
         (3, 16, 2, 1, 700, 64, torch.float16, True),
-        (32, 56, 8, 1, 1152, 128, torch.bfloat16, True),   # 8,386,560 of the 8,388,608 bytes
+        (32, 56, 8, 1, 1152, 128, torch.bfloat16, True),   # streaming cluster kernel: no scratch
+        (3, 16, 1, 1, 43008, 128, torch.bfloat16, True),   # split path, 3 x 336 splits: 8,386,560 of 8,388,608 bytes
     ]
     from mserve_b200._lib import MSKV_NOALLOC_SCRATCH_BYTES
     for B, Hq, Hkv, Q, S, D, dt, with_counts in cases:
@@ -82,10 +85,10 @@ def test_noalloc_attention_matches_workspace_entry_point(built_lib, seed):
 def test_noalloc_attention_rejects_oversized_shape(built_lib):
     from mserve_b200._lib import MSKV_ERR_RANGE
     fn = _noalloc()
-    B, Hq, Hkv, S, D = 32, 56, 8, 1153, 128     # one split more than the largest case above: 9,318,400 bytes
+    B, Hq, Hkv, S, D = 3, 16, 1, 43009, 128     # one split more per segment than the widest case above: 8,411,520 bytes
+    # every declared row is allocated, so the call could not read past a buffer even if it ran
     q = torch.zeros(B, Hq, 1, D, dtype=torch.bfloat16, device="cuda")
-    k = torch.zeros(B, Hkv, 1, D, dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros(B, Hkv, S, D, dtype=torch.bfloat16, device="cuda")
     out = torch.zeros_like(q)
     d = _desc(q, k, k, None, out)
-    d.num_selected = S                              # refused before any kernel reads K/V
     assert fn(C.byref(d), C.c_void_p(torch.cuda.current_stream().cuda_stream)) == MSKV_ERR_RANGE
