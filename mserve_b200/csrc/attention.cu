@@ -424,6 +424,14 @@ __device__ __forceinline__ void ac_tma_load(uint32_t dst, const CUtensorMap* map
                ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar) : "memory");
 }
 
+// Transpose of an 8x8 matrix of 16-bit values held one row-pair per thread (the mma.sync
+// C/A fragment layout): thread (g, tig) receives elements (2 tig, g) and (2 tig + 1, g).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 // 2^x by the SFU (ex2.approx.ftz: relative error about 2^-22; 2^-inf = 0).
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -459,7 +467,7 @@ __device__ __forceinline__ int ac_swz(int row, int c) {
   return (c >> 3) * (kAcBlock * 128) + row * 128 + (((c & 7) ^ (row & 7)) << 4);
 }
 
-template <bool BF16, int D>
+template <bool BF16, int D, bool NARROW>
 __global__ void __launch_bounds__(kAcWarps * 32, 2)
     attn_cluster_kernel(const AttnDev a, const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv) {
   allow_dependents();
@@ -536,23 +544,36 @@ __global__ void __launch_bounds__(kAcWarps * 32, 2)
     *reinterpret_cast<uint4*>(sQ + r * SH::ROWP + c * 16) = qv[k];
   }
   __syncthreads();
-  uint32_t qa[KS][4];
+  // Q fragments.  Wide (9..16 query rows): Q is the A operand (query rows on M = 16).  Narrow
+  // (<= 8 query rows): the block's 16 selected rows go on M and the query rows on N = 8, so no
+  // MMA row is padding: S^T = K·Q^T and O^T = V^T·P^T, Q the B operand.
+  constexpr int NA = NARROW ? D / 16 : D / 8;          // accumulator tiles of O (or O^T)
+  uint32_t qf[KS][NARROW ? 2 : 4];
 #pragma unroll
-  for (int kk = 0; kk < KS; ++kk) {
-    const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
-    const int col = kk * 16 + 8 * (lane >> 4);
-    ldsm_x4(qa[kk], sQ + row * SH::ROWP + col * 2);
+  for (int kk = 0; kk < KS; kk += (NARROW ? 2 : 1)) {
+    if constexpr (NARROW) {
+      uint32_t t[4];
+      ldsm_x4(t, sQ + (lane & 7) * SH::ROWP + (2 * kk + (lane >> 3)) * 16);
+      qf[kk][0] = t[0];
+      qf[kk][1] = t[1];
+      qf[kk + 1][0] = t[2];
+      qf[kk + 1][1] = t[3];
+    } else {
+      const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+      ldsm_x4(qf[kk], sQ + row * SH::ROWP + (2 * kk + (lane >> 4)) * 16);
+    }
   }
 
   const float sl2 = a.scale * 1.4426950408889634f;     // exponent base 2: exp(x) = 2^(x log2 e)
-  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
-  float oacc[NT][4];
+  // running max / normaliser of the thread's two query rows: wide, rows g and g + 8; narrow,
+  // query columns 2 tig and 2 tig + 1
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float acc[NA][4];
 #pragma unroll
-  for (int n = 0; n < NT; ++n)
+  for (int n = 0; n < NA; ++n)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) oacc[n][e] = 0.f;
+    for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
   bool ok = true;
-  const bool hi_rows = nr > 8;                         // query rows 8..15 exist
   for (int i = 0; i < nw; ++i) {
     const int s = i % kAcStages;
     uint32_t done = 0;
@@ -579,95 +600,129 @@ __global__ void __launch_bounds__(kAcWarps * 32, 2)
       }
       __syncwarp();
     }
-    // S = Q·Kᵀ over the block's 16 rows: n-tile j covers rows 8j .. 8j+7; even and odd k-steps
-    // accumulate separately (two short dependency chains per n-tile instead of one long one)
-    float sacc[2][4], sodd[2][4];
+    // scores: sc[e] of the thread's C fragment, scaled to base 2, masked past the block's rows.
+    // Wide: C = S (query g / g+8 x block rows 8j + 2 tig + {0,1}), two n-tiles j.  Narrow:
+    // C = S^T (block rows g / g+8 x query columns 2 tig + {0,1}).  K-steps accumulate in
+    // separate chains and are summed at the end.
+    constexpr int NJ = NARROW ? 1 : 2;
+    constexpr int CH = NARROW ? 4 : 2;                 // accumulation chains per n-tile
+    float sacc[NJ][CH][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int j = 0; j < NJ; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) sacc[j][e] = sodd[j][e] = 0.f;
+      for (int c = 0; c < CH; ++c)
 #pragma unroll
-    for (int kk = 0; kk < KS; kk += 2) {
+        for (int e = 0; e < 4; ++e) sacc[j][c][e] = 0.f;
+    if constexpr (NARROW) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        uint32_t kb[4];
-        const int row = 8 * j + (lane & 7);
-        ldsm_x4(kb, sK + ac_swz(row, 2 * kk + (lane >> 3)));
-        mma16816<BF16>(sacc[j], qa[kk], kb[0], kb[1]);
-        mma16816<BF16>(sodd[j], qa[kk + 1], kb[2], kb[3]);
+      for (int kk = 0; kk < KS; ++kk) {
+        uint32_t ka[4];
+        const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+        ldsm_x4(ka, sK + ac_swz(row, 2 * kk + (lane >> 4)));
+        mma16816<BF16>(sacc[0][kk % CH], ka, qf[kk][0], qf[kk][1]);
+      }
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < KS; kk += 2) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint32_t kb[4];
+          ldsm_x4(kb, sK + ac_swz(8 * j + (lane & 7), 2 * kk + (lane >> 3)));
+          mma16816<BF16>(sacc[j][0], qf[kk], kb[0], kb[1]);
+          mma16816<BF16>(sacc[j][1], qf[kk + 1], kb[2], kb[3]);
+        }
       }
     }
-    // online softmax in base 2: rows g (e < 2) and g + 8 (e >= 2); the four lanes of a group
-    // share a row.  With at most 8 query rows (hi_rows false) rows g + 8 are padding: their
-    // probabilities are set to 0 and nothing else is computed for them.
-    float bm_lo = -INFINITY, bm_hi = -INFINITY;
+    float sc[NJ][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < NJ; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int col = 8 * j + 2 * tig + (e & 1);
-        const float v = col < vrows ? (sacc[j][e] + sodd[j][e]) * sl2 : -INFINITY;
-        sacc[j][e] = v;
-        if (e < 2) bm_lo = fmaxf(bm_lo, v);
-        else bm_hi = fmaxf(bm_hi, v);
+        float v = 0.f;
+#pragma unroll
+        for (int c = 0; c < CH; ++c) v += sacc[j][c][e];
+        const int brow = NARROW ? g + 8 * (e >> 1) : 8 * j + 2 * tig + (e & 1);   // block row of the value
+        sc[j][e] = brow < vrows ? v * sl2 : -INFINITY;
+      }
+    // online softmax.  Query row q(e) of value e: wide, e >> 1 (g or g + 8); narrow, e & 1.
+    float bm[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int q = NARROW ? (e & 1) : (e >> 1);
+        bm[q] = fmaxf(bm[q], sc[j][e]);
+      }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if constexpr (NARROW) {                          // across the 8 groups holding the block rows
+        bm[q] = fmaxf(bm[q], __shfl_xor_sync(0xffffffffu, bm[q], 4));
+        bm[q] = fmaxf(bm[q], __shfl_xor_sync(0xffffffffu, bm[q], 8));
+        bm[q] = fmaxf(bm[q], __shfl_xor_sync(0xffffffffu, bm[q], 16));
+      } else {                                         // across the 4 lanes sharing a query row
+        bm[q] = fmaxf(bm[q], __shfl_xor_sync(0xffffffffu, bm[q], 1));
+        bm[q] = fmaxf(bm[q], __shfl_xor_sync(0xffffffffu, bm[q], 2));
       }
     }
-    bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, 1));
-    bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, 2));
-    if (hi_rows) {
-      bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 1));
-      bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 2));
-    }
-    const float mn_lo = fmaxf(m_lo, bm_lo);            // finite: the block has a valid row
-    const float mn_hi = hi_rows ? fmaxf(m_hi, bm_hi) : m_hi;
-    const bool moved = __any_sync(0xffffffffu, mn_lo != m_lo || mn_hi != m_hi);
-    float p_lo = 0.f, p_hi = 0.f;
+    const float mn0 = fmaxf(m[0], bm[0]), mn1 = fmaxf(m[1], bm[1]);   // finite: the block has a row
+    const bool moved = __any_sync(0xffffffffu, mn0 != m[0] || mn1 != m[1]);
+    float ps[2] = {0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < NJ; ++j)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        sacc[j][e] = ex2(sacc[j][e] - mn_lo);          // masked: 2^-inf = 0
-        p_lo += sacc[j][e];
-        if (hi_rows) {
-          sacc[j][e + 2] = ex2(sacc[j][e + 2] - mn_hi);
-          p_hi += sacc[j][e + 2];
-        } else {
-          sacc[j][e + 2] = 0.f;
-        }
+      for (int e = 0; e < 4; ++e) {
+        const int q = NARROW ? (e & 1) : (e >> 1);
+        sc[j][e] = ex2(sc[j][e] - (q ? mn1 : mn0));    // masked: 2^-inf = 0
+        ps[q] += sc[j][e];
       }
-    }
     if (moved) {                                       // rescale what was summed under the old maxima
-      const float c_lo = ex2(m_lo - mn_lo);             // 0 while nothing was seen, 1 if unchanged
-      const float c_hi = hi_rows ? ex2(m_hi - mn_hi) : 1.f;
-      l_lo *= c_lo;
-      l_hi *= c_hi;
+      const float c0 = ex2(m[0] - mn0), c1 = ex2(m[1] - mn1);   // 0 while nothing was seen, 1 if unchanged
+      l[0] *= c0;
+      l[1] *= c1;
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        oacc[n][0] *= c_lo;
-        oacc[n][1] *= c_lo;
-        if (hi_rows) {
-          oacc[n][2] *= c_hi;
-          oacc[n][3] *= c_hi;
+      for (int n = 0; n < NA; ++n) {
+        if constexpr (NARROW) {
+          acc[n][0] *= c0;
+          acc[n][1] *= c1;
+          acc[n][2] *= c0;
+          acc[n][3] *= c1;
+        } else {
+          acc[n][0] *= c0;
+          acc[n][1] *= c0;
+          acc[n][2] *= c1;
+          acc[n][3] *= c1;
         }
       }
-      m_lo = mn_lo;
-      m_hi = mn_hi;
+      m[0] = mn0;
+      m[1] = mn1;
     }
-    l_lo += p_lo;
-    l_hi += p_hi;
-    // O += P·V: P as the A fragment of one 16-row k-step, V through ldmatrix.trans
-    uint32_t pa[4];
-    pa[0] = pack2<BF16>(sacc[0][0], sacc[0][1]);
-    pa[1] = pack2<BF16>(sacc[0][2], sacc[0][3]);
-    pa[2] = pack2<BF16>(sacc[1][0], sacc[1][1]);
-    pa[3] = pack2<BF16>(sacc[1][2], sacc[1][3]);
+    l[0] += ps[0];
+    l[1] += ps[1];
+    if constexpr (NARROW) {
+      // P^T (block rows x query columns, C layout) -> the B operand of O^T += V^T·P^T by one 8x8
+      // transpose per half; V^T comes in as the A operand through ldmatrix.trans
+      const uint32_t pb0 = movmatrix_trans(pack2<BF16>(sc[0][0], sc[0][1]));
+      const uint32_t pb1 = movmatrix_trans(pack2<BF16>(sc[0][2], sc[0][3]));
 #pragma unroll
-    for (int n = 0; n < NT; n += 2) {
-      uint32_t vb[4];
-      const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
-      ldsm_x4_t(vb, sV + ac_swz(row, n + (lane >> 4)));
-      mma16816<BF16>(oacc[n], pa, vb[0], vb[1]);
-      mma16816<BF16>(oacc[n + 1], pa, vb[2], vb[3]);
+      for (int mt = 0; mt < NA; ++mt) {
+        uint32_t va[4];
+        ldsm_x4_t(va, sV + ac_swz((lane & 7) + 8 * (lane >> 4), 2 * mt + ((lane >> 3) & 1)));
+        mma16816<BF16>(acc[mt], va, pb0, pb1);
+      }
+    } else {
+      // O += P·V: P as the A fragment of one 16-row k-step, V through ldmatrix.trans
+      uint32_t pa[4];
+      pa[0] = pack2<BF16>(sc[0][0], sc[0][1]);
+      pa[1] = pack2<BF16>(sc[0][2], sc[0][3]);
+      pa[2] = pack2<BF16>(sc[1][0], sc[1][1]);
+      pa[3] = pack2<BF16>(sc[1][2], sc[1][3]);
+#pragma unroll
+      for (int n = 0; n < NA; n += 2) {
+        uint32_t vb[4];
+        ldsm_x4_t(vb, sV + ac_swz((lane & 7) + 8 * ((lane >> 3) & 1), n + (lane >> 4)));
+        mma16816<BF16>(acc[n], pa, vb[0], vb[1]);
+        mma16816<BF16>(acc[n + 1], pa, vb[2], vb[3]);
+      }
     }
     __syncwarp();                                      // every lane has read the stage
     if (lane == 0 && i + kAcStages < nw) {
@@ -676,31 +731,53 @@ __global__ void __launch_bounds__(kAcWarps * 32, 2)
     }
   }
   if (!ok) {
-    m_lo = m_hi = -INFINITY;
-    l_lo = l_hi = 0.f;
+    m[0] = m[1] = -INFINITY;
+    l[0] = l[1] = 0.f;
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+    for (int n = 0; n < NA; ++n)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) oacc[n][e] = 0.f;
+      for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
   }
 #pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, o);
-    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, o);
+  for (int q = 0; q < 2; ++q) {
+    if constexpr (NARROW) {
+      l[q] += __shfl_xor_sync(0xffffffffu, l[q], 4);
+      l[q] += __shfl_xor_sync(0xffffffffu, l[q], 8);
+      l[q] += __shfl_xor_sync(0xffffffffu, l[q], 16);
+    } else {
+      l[q] += __shfl_xor_sync(0xffffffffu, l[q], 1);
+      l[q] += __shfl_xor_sync(0xffffffffu, l[q], 2);
+    }
   }
-  // the warp's partial -> its first two stages (all its loads have landed)
+  // the warp's partial -> its first two stages (all its loads have landed): O as [query row][dim]
   float* so = reinterpret_cast<float*>(wst);
+  if constexpr (NARROW) {
 #pragma unroll
-  for (int n = 0; n < NT; ++n) {
-    const int col = n * 8 + 2 * tig;
-    *reinterpret_cast<float2*>(so + g * OS + col) = make_float2(oacc[n][0], oacc[n][1]);
-    *reinterpret_cast<float2*>(so + (g + 8) * OS + col) = make_float2(oacc[n][2], oacc[n][3]);
-  }
-  if (tig == 0) {
-    s_m[warp][g] = m_lo;
-    s_m[warp][g + 8] = m_hi;
-    s_l[warp][g] = l_lo;
-    s_l[warp][g + 8] = l_hi;
+    for (int mt = 0; mt < NA; ++mt) {
+      so[(2 * tig) * OS + mt * 16 + g] = acc[mt][0];
+      so[(2 * tig + 1) * OS + mt * 16 + g] = acc[mt][1];
+      so[(2 * tig) * OS + mt * 16 + g + 8] = acc[mt][2];
+      so[(2 * tig + 1) * OS + mt * 16 + g + 8] = acc[mt][3];
+    }
+    if (g == 0) {
+      s_m[warp][2 * tig] = m[0];
+      s_m[warp][2 * tig + 1] = m[1];
+      s_l[warp][2 * tig] = l[0];
+      s_l[warp][2 * tig + 1] = l[1];
+    }
+  } else {
+#pragma unroll
+    for (int n = 0; n < NA; ++n) {
+      const int col = n * 8 + 2 * tig;
+      *reinterpret_cast<float2*>(so + g * OS + col) = make_float2(acc[n][0], acc[n][1]);
+      *reinterpret_cast<float2*>(so + (g + 8) * OS + col) = make_float2(acc[n][2], acc[n][3]);
+    }
+    if (tig == 0) {
+      s_m[warp][g] = m[0];
+      s_m[warp][g + 8] = m[1];
+      s_l[warp][g] = l[0];
+      s_l[warp][g + 8] = l[1];
+    }
   }
   __syncthreads();
   // four warps -> the CTA's partial (warp 0's third stage, which no warp uses any more): one pass,
@@ -938,10 +1015,10 @@ static void cluster_plan(const mskv_attn_desc* d, ClusterPlan* p) {
   p->use = true;
 }
 
-template <bool BF16, int D>
+template <bool BF16, int D, bool NARROW>
 static int launch_cluster(const AttnDev& a, const mskv_attn_desc* d, const ClusterPlan& p, cudaStream_t st) {
   int rc;
-  const void* kern = (const void*)attn_cluster_kernel<BF16, D>;
+  const void* kern = (const void*)attn_cluster_kernel<BF16, D, NARROW>;
   rc = ensure_smem_limit(kern, AcShape<D>::SMEM, "mskv_sparse_attention");
   if (rc) return rc;
   const int64_t blocks = (int64_t)d->batch * d->kv_heads * p.cs;
@@ -958,7 +1035,7 @@ static int launch_cluster(const AttnDev& a, const mskv_attn_desc* d, const Clust
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = p.cs > 1 ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_cluster_kernel<BF16, D>, a, p.tk, p.tv);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_cluster_kernel<BF16, D, NARROW>, a, p.tk, p.tv);
   if (e != cudaSuccess) return cuda_status(e, "mskv_sparse_attention cluster launch");
   return after_launch("mskv_sparse_attention");
 }
@@ -1005,8 +1082,12 @@ extern "C" int mskv_sparse_attention(const mskv_attn_desc* d, void* stream) {
     a.splits = cp.cs;
     a.rps = cp.rps;
     const bool bf = d->dtype == MSKV_DT_BF16;
-    if (d->head_dim == 128) return bf ? launch_cluster<true, 128>(a, d, cp, st) : launch_cluster<false, 128>(a, d, cp, st);
-    return bf ? launch_cluster<true, 64>(a, d, cp, st) : launch_cluster<false, 64>(a, d, cp, st);
+    if (a.nr <= 8) {
+      if (d->head_dim == 128) return bf ? launch_cluster<true, 128, true>(a, d, cp, st) : launch_cluster<false, 128, true>(a, d, cp, st);
+      return bf ? launch_cluster<true, 64, true>(a, d, cp, st) : launch_cluster<false, 64, true>(a, d, cp, st);
+    }
+    if (d->head_dim == 128) return bf ? launch_cluster<true, 128, false>(a, d, cp, st) : launch_cluster<false, 128, false>(a, d, cp, st);
+    return bf ? launch_cluster<true, 64, false>(a, d, cp, st) : launch_cluster<false, 64, false>(a, d, cp, st);
   }
   if (fast_path(d)) {
     const uint64_t need = mskv_attention_workspace_bytes(d);
