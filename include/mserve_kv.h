@@ -260,9 +260,14 @@ int mskv_topk(const mskv_topk_desc* d, void* stream);
  * in fp32, output in `dtype`.  K_sel/V_sel row s of (b,hk) at
  *   base + (b*kv_heads + hk)*kv_stride_seg + s*kv_stride_s (bytes).
  * q row (b,hq,i) at q + b*q_stride_b + hq*q_stride_h + i*q_stride_q (bytes), likewise out.
- * `workspace` must hold mskv_attention_workspace_bytes(d) bytes of device memory (the
- * split-sequence partial results; every launch writes all it reads, so no initialisation is
- * needed).  Launches that share a workspace must be ordered (same stream). */
+ * `workspace` must hold mskv_attention_workspace_bytes(d) bytes of device memory.  That is 0
+ * for the fast path's selections of up to 32768 rows (16-bit q/K/V, head_dim 64 or 128, at
+ * most 16 query rows per KV head, 16-byte aligned rows and strides): one kernel whose CTAs of a
+ * (b,hk) segment merge through distributed shared memory.  Wider selections use the
+ * split-sequence kernels, whose partial results live in the workspace (every launch writes all
+ * it reads, so no initialisation is needed; launches that share a workspace must be ordered on
+ * one stream).  A segment's rows are split the same way whatever the batch and the number of
+ * segments in the call, so a segment's output does not depend on the rest of the call. */
 typedef struct mskv_attn_desc {
   const void* q;
   int64_t q_stride_b;
@@ -297,10 +302,10 @@ int mskv_sparse_attention(const mskv_attn_desc* d, void* stream);
  * where they run attention (code under an allocator lock or inside another library's memory
  * pool, host frameworks that forbid cudaMalloc on the decode path, callers with no allocator
  * to hand out a workspace).  Same computation and arguments as mskv_sparse_attention, but
- * d->workspace / d->workspace_bytes are ignored: the workspace is a device array of
- * MSKV_NOALLOC_ATTN_SCRATCH_BYTES built into the library, which each GPU that loads the
- * library holds until the process exits.  Shapes whose mskv_attention_workspace_bytes()
- * exceeds that size are rejected with MSKV_ERR_RANGE.  The first call on a device looks up
+ * d->workspace / d->workspace_bytes are ignored: shapes that need a workspace (selections
+ * wider than 32768 rows) get a device array of MSKV_NOALLOC_ATTN_SCRATCH_BYTES built into the
+ * library, which each GPU that loads the library holds until the process exits.  Shapes whose
+ * mskv_attention_workspace_bytes() exceeds that size are rejected with MSKV_ERR_RANGE.  The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress) with that device current, and looks it up
  * again when the device's context has been re-created since (cudaDeviceReset); make that
  * first call before any stream capture.  Every call on a device shares the array and
