@@ -169,29 +169,6 @@ constexpr int kBulkMaxRow = kBulkBank / 2;           // K and V rows of one tile
 // measured 0.907 of the link with bulk copies against 0.919 with loads, while whole-token rows
 // (1-2 KiB) gain from them, most in small transfers and in write-back.
 constexpr int kBulkMinRow = 1024;
-constexpr int kBulkWaitIters = 1 << 22;
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ bool bulk_wait(uint32_t bar, uint32_t parity) {
-  for (int it = 0; it < kBulkWaitIters; ++it) {
-    uint32_t done;
-    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                 : "=r"(done) : "r"(bar), "r"(parity) : "memory");
-    if (done) return true;
-  }
-  return false;
-}
-
-__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(dst_smem), "l"(src), "r"(bytes), "r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void bulk_store(void* dst, uint32_t src_smem, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src_smem), "r"(bytes)
-               : "memory");
-}
 
 // One tile's rows as the warp sees them: lane i holds row i's offsets (valid for i < n).
 struct BulkTile {

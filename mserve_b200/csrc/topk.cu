@@ -93,6 +93,42 @@ __device__ __forceinline__ void load_keys(const TopkDev& a, const float* row0, i
   }
 }
 
+// load_keys for a selection of one score row whose first key is 16-byte aligned: float4 loads,
+// NL in flight per thread (the same keys, so the same histogram).
+template <int NL>
+__device__ __forceinline__ void load_keys_row4(const TopkDev& a, const float* src, int n, uint32_t* s_keys,
+                                               int tid, int nthreads, uint32_t* hist, int hist_shift) {
+  const int n4 = n >> 2;
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  uint4* k4 = reinterpret_cast<uint4*>(s_keys);
+  for (int base = tid; base < n4; base += NL * nthreads) {
+    float4 v[NL];
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = base + u * nthreads;
+      v[u] = i < n4 ? s4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = base + u * nthreads;
+      if (i < n4) {
+        const uint4 key = make_uint4(order_key(v[u].x * a.scale), order_key(v[u].y * a.scale),
+                                     order_key(v[u].z * a.scale), order_key(v[u].w * a.scale));
+        k4[i] = key;
+        atomicAdd(&hist[key.x >> hist_shift], 1u);
+        atomicAdd(&hist[key.y >> hist_shift], 1u);
+        atomicAdd(&hist[key.z >> hist_shift], 1u);
+        atomicAdd(&hist[key.w >> hist_shift], 1u);
+      }
+    }
+  }
+  for (int i = 4 * n4 + tid; i < n; i += nthreads) {
+    const uint32_t key = order_key(src[i] * a.scale);
+    s_keys[i] = key;
+    atomicAdd(&hist[key >> hist_shift], 1u);
+  }
+}
+
 __device__ __forceinline__ void put(const TopkDev& a, int64_t j, int64_t pos, int64_t tok) {
   if (a.out64) reinterpret_cast<int64_t*>(a.out)[j * a.os + pos] = tok;
   else reinterpret_cast<int32_t*>(a.out)[j * a.os + pos] = (int32_t)tok;
@@ -239,14 +275,14 @@ constexpr int kSmWarps = kSmThreads / 32;
 constexpr int kSmMaxKeys = 48 * 1024;  // a multiple of 4: the buffer holds whole 4-key units
 constexpr int kSmBins = 4096;
 
-// Finds the bin holding the krem-th largest key of the histogram (bins ordered by value);
-// sets *prefix |= bin << shift and *krem to the rank within that bin.  Every thread calls it.
 // Finds the bin holding the krem-th largest key (bins ordered by value) from the 4 bin counts
 // c[0..3] each thread owns (bins 4t .. 4t+3); sets prefix |= bin << shift and krem to the rank
-// within that bin.  Every thread of the CTA calls it.
+// within that bin, and full when that rank is the bin's count: every key of the bin is then
+// selected, and so is every key whose digits so far are at least the prefix.  Every thread of
+// the CTA calls it.
 __device__ __forceinline__ void sm_digit_search(const uint32_t (&c)[4], int shift, uint32_t* s_wsuf,
-                                                uint32_t* s_prefix, uint32_t* s_krem, uint32_t& prefix,
-                                                uint32_t& krem) {
+                                                uint32_t* s_prefix, uint32_t* s_krem, uint32_t* s_full,
+                                                uint32_t& prefix, uint32_t& krem, bool& full) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t own = c[0] + c[1] + c[2] + c[3];
   uint32_t suf = own;  // inclusive suffix over the lanes of the warp
@@ -272,15 +308,17 @@ __device__ __forceinline__ void sm_digit_search(const uint32_t (&c)[4], int shif
   uint32_t cum = s_wsuf[warp] + (suf - own);  // keys in bins above this thread's bins
 #pragma unroll
   for (int i = 3; i >= 0; --i) {
-    if (cum < krem && cum + c[i] >= krem) {
+    if (cum < krem && cum + c[i] >= krem) {   // exactly one (thread, bin) holds the krem-th key
       *s_prefix = prefix | ((uint32_t)(4 * tid + i) << shift);
       *s_krem = krem - cum;
+      *s_full = cum + c[i] == krem;
     }
     cum += c[i];
   }
   __syncthreads();
   prefix = *s_prefix;
   krem = *s_krem;
+  full = *s_full != 0;
 }
 
 // The thread's 4 bins of a histogram, summed over the NCTA CTAs of the cluster (distributed
@@ -322,7 +360,7 @@ __global__ void __launch_bounds__(kSmThreads) topk_smem_kernel(const TopkDev a) 
   __shared__ uint32_t s_wsuf[kSmWarps];
   __shared__ uint64_t s_wcnt[kSmWarps];
   __shared__ uint64_t s_cnt;
-  __shared__ uint32_t s_prefix, s_krem;
+  __shared__ uint32_t s_prefix, s_krem, s_full;
 
   const int rank = NCTA > 1 ? (int)cg::this_cluster().block_rank() : 0;
   const int64_t j = blockIdx.x / NCTA;
@@ -346,33 +384,50 @@ __global__ void __launch_bounds__(kSmThreads) topk_smem_kernel(const TopkDev a) 
     if (tid < 256) s_hist2[tid] = 0;
     __syncthreads();
     // keys into shared memory; digit 0 (bits 31..20) histogrammed on the way
-    load_keys<16>(a, row0, lo, m, s_keys, tid, kSmThreads, s_hist0, 20);
+    if (a.rows_per_sel == 1 && (reinterpret_cast<uintptr_t>(row0 + lo) & 15) == 0)
+      load_keys_row4<4>(a, row0 + lo, m, s_keys, tid, kSmThreads, s_hist0, 20);
+    else
+      load_keys<16>(a, row0, lo, m, s_keys, tid, kSmThreads, s_hist0, 20);
     cta_group_sync<NCTA>();
     uint32_t prefix = 0, krem = (uint32_t)K, c[4];
+    bool full = false;
     cluster_bins<NCTA>(c, s_hist0, kSmBins);
-    sm_digit_search(c, 20, s_wsuf, &s_prefix, &s_krem, prefix, krem);
-    // digit 1: bits 19..8 of the keys whose top 12 bits match
-    for (int u = tid; u < m4; u += kSmThreads) {
-      const uint4 kv = keys4[u];
-      const uint32_t k4[4] = {kv.x, kv.y, kv.z, kv.w};
+    sm_digit_search(c, 20, s_wsuf, &s_prefix, &s_krem, &s_full, prefix, krem, full);
+    if (full) {
+      // the bitmaps below reuse s_hist0, which the peer CTAs read for digit 0
+      if constexpr (NCTA > 1) cta_group_sync<NCTA>();
+    } else {
+      // digit 1: bits 19..8 of the keys whose top 12 bits match
+      for (int u = tid; u < m4; u += kSmThreads) {
+        const uint4 kv = keys4[u];
+        const uint32_t k4[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (4 * u + e < m && (k4[e] >> 20) == (prefix >> 20)) atomicAdd(&s_hist1[(k4[e] >> 8) & 0xfffu], 1u);
+        for (int e = 0; e < 4; ++e)
+          if (4 * u + e < m && (k4[e] >> 20) == (prefix >> 20)) atomicAdd(&s_hist1[(k4[e] >> 8) & 0xfffu], 1u);
+      }
+      cta_group_sync<NCTA>();
+      cluster_bins<NCTA>(c, s_hist1, kSmBins);
+      sm_digit_search(c, 8, s_wsuf, &s_prefix, &s_krem, &s_full, prefix, krem, full);
     }
-    cta_group_sync<NCTA>();
-    cluster_bins<NCTA>(c, s_hist1, kSmBins);
-    sm_digit_search(c, 8, s_wsuf, &s_prefix, &s_krem, prefix, krem);
-    // digit 2: bits 7..0 of the keys whose top 24 bits match
-    for (int u = tid; u < m4; u += kSmThreads) {
-      const uint4 kv = keys4[u];
-      const uint32_t k4[4] = {kv.x, kv.y, kv.z, kv.w};
+    if (!full) {
+      // digit 2: bits 7..0 of the keys whose top 24 bits match
+      for (int u = tid; u < m4; u += kSmThreads) {
+        const uint4 kv = keys4[u];
+        const uint32_t k4[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (4 * u + e < m && (k4[e] >> 8) == (prefix >> 8)) atomicAdd(&s_hist2[k4[e] & 0xffu], 1u);
+        for (int e = 0; e < 4; ++e)
+          if (4 * u + e < m && (k4[e] >> 8) == (prefix >> 8)) atomicAdd(&s_hist2[k4[e] & 0xffu], 1u);
+      }
+      cta_group_sync<NCTA>();
+      cluster_bins<NCTA>(c, s_hist2, 256);
+      sm_digit_search(c, 0, s_wsuf, &s_prefix, &s_krem, &s_full, prefix, krem, full);
+    } else {
+      // Stopped early: the selection is every key at or above the prefix (its unresolved low
+      // bits are zero).  Some key lies below it (K < n), so prefix > 0, and "above prefix - 1,
+      // no ties kept" describes the same set to the compaction.
+      prefix -= 1u;
+      krem = 0;
     }
-    cta_group_sync<NCTA>();
-    cluster_bins<NCTA>(c, s_hist2, 256);
-    sm_digit_search(c, 0, s_wsuf, &s_prefix, &s_krem, prefix, krem);
 
     // Ordered compaction through bitmaps.  Word q covers this CTA's keys [32q, 32q+32), bit i =
     // key lo + 32q + i: G_q marks keys above the threshold key, E_q keys equal to it (one

@@ -229,3 +229,79 @@ def test_topk_summed_rows_cluster_path(built_lib):
     np.testing.assert_array_equal(cnt, rcnt)
     for j in range(B):
         np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
+
+
+def _run_topk_exact(rows: torch.Tensor, K: int, R: int):
+    from mserve_b200 import ops
+    got, cnt = ops.topk(rows.cuda(), top_k=K, recent=R)
+    ref, rcnt = ko.select_topk_window(rows.numpy(), top_k=K, recent=R)
+    got, cnt = got.cpu().numpy(), cnt.cpu().numpy()
+    np.testing.assert_array_equal(cnt, rcnt)
+    for j in range(rows.shape[0]):
+        np.testing.assert_array_equal(got[j, :cnt[j]], ref[j])
+
+
+@pytest.mark.parametrize("T", [16000, 70000, 140000, 300000])   # 1, 2, 4 and 8 CTAs per selection
+@pytest.mark.parametrize("stop", ["digit0", "digit1"])
+def test_topk_stops_at_a_full_bin(built_lib, T, stop):
+    """Selections whose k-th key sits in a bin that is selected in full, so the radix passes stop
+    after the first (digit0) or the second (digit1) digit: exact against the oracle."""
+    g = torch.Generator().manual_seed(T + (stop == "digit1"))
+    S, K, R = 3, T // 10, 32
+    rows = torch.rand(S, T, generator=g) * 2 - 1                      # [-1, 1): below every selected key
+    for j in range(S):
+        top = torch.randperm(T - R, generator=g)[:K]
+        if stop == "digit0":
+            # all K selected keys in one 12-bit bin: [1024, 1152)
+            rows[j, top] = 1024 + 128 * torch.rand(K, generator=g) * 0.999
+        else:
+            # K - 3 keys far above; three equal keys at 1.6 (24-bit bin full); the rest of the
+            # candidates share 1.6's 12-bit bin [1.5, 1.625) below it, or lie in [-1, 1)
+            rows[j, top[:K - 3]] = 2048 + 2048 * torch.rand(K - 3, generator=g) * 0.999
+            rows[j, top[K - 3:]] = 1.6
+            same_bin = torch.randperm(T - R, generator=g)[: T // 4]
+            same_bin = same_bin[~torch.isin(same_bin, top)]
+            rows[j, same_bin] = 1.5 + 0.09 * torch.rand(len(same_bin), generator=g)
+    _run_topk_exact(rows, K, R)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("method", [0, 1])
+def test_scores_equal_with_and_without_l2_prefetch(built_lib, dtype, D, method):
+    """Keys with rows back to back (the streaming kernel prefetches them into L2) and the same
+    keys at a two-row token stride (no prefetch) give bit-identical scores: paged with
+    scattered and unmapped pages and ragged lengths, and strided."""
+    from mserve_b200 import ops
+    g = torch.Generator().manual_seed(D + method)
+    dev = torch.device("cuda")
+    B, Hq, Hkv, ps, maxp = 3, 12, 4, 16, 40
+    P = B * maxp
+    q = torch.randn(B, Hq, D, generator=g).to(dtype).to(dev)
+    pool = torch.randn(P, Hkv, ps, D, generator=g).to(dtype)
+    perm = torch.randperm(P, generator=g).to(torch.int32).view(B, maxp)
+    perm[1, 7] = -1                                                   # an unmapped page: -inf scores
+    lens = torch.tensor([maxp * ps, 333, 17], dtype=torch.int32).to(dev)
+    T = maxp * ps
+    wide = torch.zeros(P, Hkv, ps, 2, D, dtype=dtype)
+    wide[:, :, :, 0] = pool
+    outs = []
+    for k_pool in (pool.to(dev), wide.to(dev).view(P, Hkv, 2 * ps, D)[:, :, ::2]):
+        out = torch.full((B, Hkv, T), float("nan"), device=dev)
+        rows = ops.paged_rows(k_pool, None, perm.to(dev), len_=lens)
+        ops.score(q, rows, batch=B, kv_heads=Hkv, max_tokens=T, out=out, method=method)
+        outs.append(out.cpu())
+    assert torch.equal(outs[0].isnan(), outs[1].isnan())
+    assert torch.equal(torch.nan_to_num(outs[0], nan=7.0), torch.nan_to_num(outs[1], nan=7.0))
+    assert torch.isinf(outs[0][1, :, 7 * ps:8 * ps]).all()
+    # strided [B, Hkv, T, D] (capacity view) against the same keys at a two-row stride
+    k = torch.randn(B, Hkv, 2 * T, D, generator=g).to(dtype).to(dev)
+    k2 = torch.zeros(B, Hkv, T, 2, D, dtype=dtype, device=dev)
+    k2[:, :, :, 0] = k[:, :, :T]
+    res = []
+    for kv in (k[:, :, :T], k2.view(B, Hkv, 2 * T, D)[:, :, ::2]):
+        out = torch.empty(B, Hkv, T, device=dev)
+        ops.score(q, ops.strided_rows(kv, None), batch=B, kv_heads=Hkv, max_tokens=T, out=out, method=method)
+        res.append(out.cpu())
+    assert torch.equal(res[0], res[1])
+    ops.check_status(dev, "score parity with and without prefetch")
