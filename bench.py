@@ -97,7 +97,8 @@ def parse():
     ap.add_argument("--no-exchange", action="store_true", help="skip the shared-selection exchange timing")
     ap.add_argument("--no-parity", action="store_true", help="skip the per-rank check against the unsharded layer")
     ap.add_argument("--no-extra", action="store_true",
-                    help="skip the 32B-shape decode (4 layers) and the transfer-sweep points of the line")
+                    help="skip the 32B-shape decode (4 layers), the 34B multi-turn decode (2 layers) and the "
+                         "transfer-sweep points of the line")
     ap.add_argument("--chunks", type=int, default=4, help="sequence chunks pipelined per layer")
     ap.add_argument("--gather-ctas", type=int, default=0,
                     help="CTAs of each host-memory gather (0: the library's default bound)")
@@ -763,6 +764,44 @@ def extra_qwen32b(world, rank, dev, steps, warmup, chunks, layers=4):
             "workload": WORKLOADS["qwen32b"][1] + f" ({layers} of its 64 layers)"}
 
 
+def extra_llava34b(world, rank, dev, steps, warmup, chunks, layers=2):
+    """The LLaVA-v1.6-34B multi-turn shape (32 sequences of 4096-65536 tokens, 56/8 heads), its KV
+    heads split over the ranks like the main workload, `layers` of its 60 layers: one timed append
+    turn of 2880 image + 64 text tokens per sequence (16-token HBM key pages and host
+    write-through), then the captured decode step selecting the top ceil(10% of L_b) per
+    (sequence, KV head); whole-job GB/s and ms (max over ranks)."""
+    from mserve_b200 import ops, parallel
+    wl = dict(WORKLOADS["llava34b"][0], layers=layers)
+    plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank)
+    eng, q = build_engine(wl, plan, dev)
+    ms, host_bytes, _ = append_turn(eng, wl, plan, dev)
+    t_turn = max_over_ranks(ms * 1e-3, world)
+    host_all = sum_over_ranks(host_bytes, world)
+    out = torch.empty((wl["layers"],) + tuple(eng.buffers().out.shape), dtype=eng.dtype, device=dev)
+    g = eng.capture_decode_step(q, out, chunks=chunks)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ops.check_status(dev, "34B-shape decode")
+    t = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    total = sum_over_ranks(gathered_bytes(eng) * wl["layers"] * steps, world)
+    del g, eng, q, out
+    torch.cuda.empty_cache()
+    return {"value": total / t / 1e9, "unit": "GB/s", "ms_per_step": t / steps * 1e3, "layers": wl["layers"],
+            "of_layers": 60, "steps": steps,
+            "append_turn": {"ms": t_turn * 1e3, "host_write_bytes": host_all, "host_write_gbs": host_all / t_turn / 1e9},
+            "shard": {"kv_heads_per_rank": plan.h1 - plan.h0, "sequences_per_rank": plan.b1 - plan.b0},
+            "workload": WORKLOADS["llava34b"][1] + f" ({layers} of its 60 layers)"}
+
+
 def extra_transfer_points(world, dev, peaks):
     """Points of the transfer sweep (one token-major layer [131072, 8, 128], whole-token rows,
     uniform-random selections, seed 4) on every rank at once: gather host->HBM and write-back
@@ -936,10 +975,11 @@ def run_mserve(args, world, rank, local):
             if own_group:
                 dist.destroy_process_group()
 
-    # The 32B shape and transfer-sweep points on the same ranks (configurations 3 and 5).
+    # The 32B shape, the 34B multi-turn shape and transfer-sweep points on the same ranks.
     extra = None
     if not args.no_extra:
         extra = {"qwen32b_decode": extra_qwen32b(world, rank, dev, args.steps, args.warmup, args.chunks),
+                 "llava34b_decode": extra_llava34b(world, rank, dev, args.steps, args.warmup, args.chunks),
                  "transfer": extra_transfer_points(world, dev, peaks_all)}
 
     # CPU baseline: the C restatement on this host's cores, rank 0 at N=1 only
