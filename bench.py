@@ -388,9 +388,13 @@ def workload_config(wl, name, world, plan_desc):
 def plan_description(wl, world):
     from mserve_b200.parallel import shard_plan
     p = shard_plan(wl["batch"], wl["kv_heads"], world, 0)
-    return (f"{world} rank(s) split one problem: {p.h1 - p.h0} of {wl['kv_heads']} KV heads x {p.b1 - p.b0} of "
-            f"{wl['batch']} sequences per rank, each rank gathering over its own host link, no collective on "
-            "the data path")
+    if p.seq_groups == 1:
+        seqs = f"{p.b1 - p.b0} of {wl['batch']} sequences per rank"
+    else:
+        seqs = (f"the {wl['batch']} sequences over {p.seq_groups} sequence groups in proportion to each group's "
+                "slowest measured host-link rate (evenly when the links are equally fast)")
+    return (f"{world} rank(s) split one problem: {p.h1 - p.h0} of {wl['kv_heads']} KV heads x {seqs}, each rank "
+            "gathering over its own host link, no collective on the data path")
 
 
 # ------------------------------------------------------------------------------------- CPU path
@@ -850,7 +854,21 @@ def run_mserve(args, world, rank, local):
     if args.layers:
         wl["layers"] = args.layers
     L = wl["layers"]
+    # Link rates first: with more ranks than KV heads, each sequence group takes sequences in
+    # proportion to the slowest concurrent host-link rate among its ranks (equal shares would
+    # all wait for the slowest link; equally fast links give the even split).
+    barrier(world)
+    peaks = pcie_peaks(dev, world)
+    h2d_ranks = gather_objects(peaks["h2d"], world)
     plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank)
+    seq_weights = None
+    if plan.seq_groups > 1:
+        seq_weights = [min(h2d_ranks[r] for r in plan.group_ranks(g)) for g in range(plan.seq_groups)]
+        plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank, seq_weights=seq_weights)
+    seq_split_counts = (parallel.seq_split(wl["batch"], seq_weights) if seq_weights
+                        else [wl["batch"] // plan.seq_groups] * plan.seq_groups)
+    group_rates = seq_weights or [min(h2d_ranks[r] for r in plan.group_ranks(g)) for g in range(plan.seq_groups)]
+    split_bound_gbs = wl["batch"] * plan.head_groups / max(n / r for n, r in zip(seq_split_counts, group_rates))
     eng, q = build_engine(wl, plan, dev)
     eng.host_link_ctas = args.gather_ctas
     turn = None
@@ -864,8 +882,6 @@ def run_mserve(args, world, rank, local):
                         "through to the pinned host store (mskv_copy_rows), CUDA events, max over ranks"}
     bufs = eng.buffers()
     numa_node = topology.numa_node(dev)
-    barrier(world)
-    peaks = pcie_peaks(dev, world)
     peaks_all = {"h2d_sum": sum_over_ranks(peaks["h2d"], world), "d2h_sum": sum_over_ranks(peaks["d2h"], world),
                  "h2d_min_rank": min_over_ranks(peaks["h2d"], world),
                  "h2d_per_rank": gather_objects(round(peaks["h2d"], 2), world),
@@ -1080,7 +1096,10 @@ def run_mserve(args, world, rank, local):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": workload_config(wl, name, world, plan_description(wl, world)),
             "shard": {"kv_heads_per_rank": plan.h1 - plan.h0, "sequences_per_rank": plan.b1 - plan.b0,
-                      "head_groups": plan.head_groups, "sequence_groups": plan.seq_groups},
+                      "head_groups": plan.head_groups, "sequence_groups": plan.seq_groups,
+                      "sequences_per_group": seq_split_counts,
+                      "sequence_split": ("in proportion to each sequence group's slowest concurrent H2D link rate "
+                                         f"{[round(x, 2) for x in seq_weights]} GB/s") if seq_weights else "even"},
             "parity": parity,
             "roofline": roofline, "roofline_select": roofline_select,
             "breakdown_ms_per_layer": {"score_topk": sel_ms, "gather": gat_ms, "gather_max_over_ranks": gat_ms_max,
@@ -1096,6 +1115,9 @@ def run_mserve(args, world, rank, local):
             "gather_frac_of_concurrent_h2d_peak_whole_step": value / peaks_all["h2d_sum"],
             # equal shares finish with the slowest rank: its concurrent link rate x N bounds the job
             "gather_frac_of_slowest_rank_peak_x_n": value / (peaks_all["h2d_min_rank"] * world),
+            # the job's bound for the split it ran: every group's ranks move its share at the
+            # group's slowest link rate, and the slowest group sets the step
+            "gather_frac_of_split_bound": value / split_bound_gbs,
             "host_placement": {"numa_node": numa_node, "local_cpus": len(eng.host_cpus),
                                "note": "host store allocated on the GPU's local CPUs (0: placement left to the system)"},
             "shared_selection": shared,

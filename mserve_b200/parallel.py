@@ -72,20 +72,51 @@ class ShardPlan:
         return list(range(seq_group * self.head_groups, (seq_group + 1) * self.head_groups))
 
 
-def shard_plan(batch: int, kv_heads: int, world: int, rank: int) -> ShardPlan:
-    """Splits batch x kv_heads (sequence, KV head) pairs evenly over `world` ranks (see ShardPlan)."""
+def seq_split(batch: int, weights) -> list:
+    """Sequences per sequence group for groups that move rows at the given relative rates: at
+    least one each, the rest handed out one at a time to the group whose time (sequences / rate)
+    grows least, which minimises the largest time.  Equal rates give an even split (ties go to
+    the lower group)."""
+    w = [float(x) for x in weights]
+    if not w or any(not x > 0 for x in w):
+        raise ValueError(f"sequence-group rates must be positive, got {weights}")
+    if batch < len(w):
+        raise ValueError(f"{batch} sequences cannot cover {len(w)} sequence groups")
+    n = [1] * len(w)
+    for _ in range(batch - len(w)):
+        g = min(range(len(w)), key=lambda i: ((n[i] + 1) / w[i], i))
+        n[g] += 1
+    return n
+
+
+def shard_plan(batch: int, kv_heads: int, world: int, rank: int, seq_weights=None) -> ShardPlan:
+    """Splits batch x kv_heads (sequence, KV head) pairs over `world` ranks (see ShardPlan).
+
+    The KV heads always split evenly.  When there are more ranks than KV heads the sequences are
+    split too: evenly, or, with seq_weights (one relative rate per sequence group, e.g. the
+    slowest measured host-link rate among the group's ranks), by seq_split so that groups on
+    faster links take more sequences.  Every rank must pass the same weights."""
     if world <= 0 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} of world {world}")
     hg = min(world, kv_heads)
     if kv_heads % hg or world % hg:
         raise ValueError(f"{world} ranks cannot split {kv_heads} KV heads evenly")
     sg = world // hg
-    if batch % sg:
-        raise ValueError(f"{world} ranks over {kv_heads} KV heads leave {sg} sequence groups, which do not "
-                         f"split {batch} sequences evenly")
-    hl, bl = kv_heads // hg, batch // sg
+    hl = kv_heads // hg
     hi, si = rank % hg, rank // hg
-    return ShardPlan(world, rank, hg, sg, si * bl, (si + 1) * bl, hi * hl, (hi + 1) * hl)
+    if seq_weights is None or sg == 1:
+        if batch % sg:
+            raise ValueError(f"{world} ranks over {kv_heads} KV heads leave {sg} sequence groups, which do not "
+                             f"split {batch} sequences evenly")
+        bl = batch // sg
+        b0, b1 = si * bl, (si + 1) * bl
+    else:
+        if len(seq_weights) != sg:
+            raise ValueError(f"{len(seq_weights)} sequence-group weights for {sg} sequence groups")
+        counts = seq_split(batch, seq_weights)
+        b0 = sum(counts[:si])
+        b1 = b0 + counts[si]
+    return ShardPlan(world, rank, hg, sg, b0, b1, hi * hl, (hi + 1) * hl)
 
 
 def exchange_head_scores(local: torch.Tensor, gathered: torch.Tensor, group=None) -> torch.Tensor:

@@ -288,3 +288,48 @@ def test_shard_plan_rejects_uneven_splits():
         shard_plan(7, 4, 8, 0)          # 8 ranks over 4 heads: 2 sequence groups of 7 sequences
     with pytest.raises(ValueError):
         shard_plan(8, 4, 8, 8)
+
+
+def test_seq_split_minimises_the_slowest_group():
+    """Sequences per sequence group by link rate: equal rates give the even split, unequal rates
+    the integer split whose largest sequences / rate is smallest (checked against every split)."""
+    import itertools
+    from mserve_b200.parallel import seq_split
+    assert seq_split(8, [55.5, 55.4]) == [4, 4]
+    assert seq_split(8, [1.0, 1.0, 1.0, 1.0]) == [2, 2, 2, 2]
+    assert seq_split(8, [23.1, 35.1]) == [3, 5]
+    for B, rates in [(8, [23.1, 35.1]), (9, [10.0, 20.0, 30.0]), (16, [5.0, 7.0, 11.0, 13.0]), (3, [1.0, 9.0, 2.0])]:
+        got = seq_split(B, rates)
+        assert sum(got) == B and min(got) >= 1
+        best = min(max(n / r for n, r in zip(c, rates))
+                   for c in itertools.product(range(1, B + 1), repeat=len(rates)) if sum(c) == B)
+        assert max(n / r for n, r in zip(got, rates)) == pytest.approx(best)
+    with pytest.raises(ValueError):
+        seq_split(1, [1.0, 1.0])
+    with pytest.raises(ValueError):
+        seq_split(8, [1.0, 0.0])
+
+
+@pytest.mark.parametrize("rates", [[23.1, 35.1], [35.1, 23.1], [30.0, 30.0]])
+def test_weighted_shard_plan_covers_every_pair_once(rates):
+    """With per-sequence-group weights every (sequence, KV head) pair is still on exactly one rank,
+    and the ranks of a sequence group hold the same sequences (the shared selection's groups)."""
+    from mserve_b200.parallel import seq_split, shard_plan
+    B, Hkv, world = 8, 4, 8
+    counts = seq_split(B, rates)
+    owner = {}
+    for r in range(world):
+        p = shard_plan(B, Hkv, world, r, seq_weights=rates)
+        assert p.b1 - p.b0 == counts[p.seq_group]
+        for q in p.group_ranks(p.seq_group):
+            o = shard_plan(B, Hkv, world, q, seq_weights=rates)
+            assert (o.b0, o.b1) == (p.b0, p.b1)
+        for b in range(p.b0, p.b1):
+            for h in range(p.h0, p.h1):
+                assert (b, h) not in owner
+                owner[(b, h)] = r
+    assert len(owner) == B * Hkv
+    # one sequence group: the weights change nothing
+    assert shard_plan(8, 4, 4, 1, seq_weights=[9.0]) == shard_plan(8, 4, 4, 1)
+    with pytest.raises(ValueError):
+        shard_plan(B, Hkv, world, 0, seq_weights=[1.0, 2.0, 3.0])
