@@ -181,10 +181,10 @@ int mskv_copy_rows(const mskv_copy_desc* d, void* stream);
  * (len[b] above max_tokens is clamped to it); tokens whose page is unmapped score -inf
  * (MSKV_STATUS_BAD_PAGE).
  * Fast path (16-bit K, head_dim in {64,128,256}, 16-byte aligned rows, page_size a multiple
- * of 8): register streaming, 8 rows per group of head_dim/8 lanes with 16-byte loads,
- * double-buffered so the next slice's loads are in flight while a slice is scored; warps share
- * the slices that hold tokens equally however ragged len[] is.  Other shapes use a 32-row
- * register kernel or a generic one. */
+ * of 8): register streaming, 8 rows per group of head_dim/8 lanes with 16-byte loads, 24
+ * warps per SM each with one slice's loads in flight; warps share the slices that hold tokens
+ * equally however ragged len[] is.  Other shapes use a 32-row register kernel or a generic
+ * one. */
 typedef struct mskv_score_desc {
   mskv_rows k;
   const void* q;

@@ -211,12 +211,13 @@ __global__ void __launch_bounds__(256) score_fast_kernel(const ScoreDev a) {
 //
 // GL = D/8 lanes own one row (one 16-byte chunk each); a group of GL lanes takes 8
 // consecutive rows per slice, so every lane issues 8 independent 16-byte loads per slice
-// (ld.global.nc with L1 bypass and a 256-byte L2 prefetch: one bf16 row), and a second
-// register buffer keeps the next slice's loads in flight while a slice is scored: 128
-// registers, 2 CTAs (16 warps) and up to 128 KB of key bytes in flight per SM.  Products use
+// (ld.global.nc with L1 bypass and a 256-byte L2 prefetch: one bf16 row) into one register
+// buffer: 80 registers, 3 CTAs (24 warps) per SM, the other warps' loads in flight while a
+// warp scores.  (Measured at the 7B and 32B decode shapes: 24 single-buffered warps per SM
+// beat 16 double-buffered ones by 2.5-4%; fewer warps with deeper buffers, shared-memory
+// staging by bulk copies or cp.async, and L2 prefetching were all slower.)  Products use
 // packed fp32x2 FMAs (two lanes of fp32 per instruction); the 8 partial dots are
-// reduce-scattered over 8 lanes and finished with xor-shuffles.  (Staging the keys in shared
-// memory -- bulk copies, or cp.async with 1.5x the bytes in flight -- measured no faster.)
+// reduce-scattered over 8 lanes and finished with xor-shuffles.
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -457,10 +458,9 @@ __device__ __forceinline__ void gqa_query(const ScoreDev& a, int b, int h, int g
   }
 }
 
-// Each warp walks its contiguous run of slices with two register buffers: the 8 loads of
-// slice s+1 are issued before slice s is scored, so every lane always has 8 loads in flight.
+// Each warp walks its contiguous run of slices: the 8 loads of a slice, then its score.
 template <typename T, int D, int METHOD, bool PAGED>
-__global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) {
+__global__ void __launch_bounds__(256, 3) score_stream_kernel(const ScoreDev a) {
   allow_dependents();  // the top-k kernel may become resident as this grid drains
   constexpr int GL = D / 8;
   static_assert(GL >= 8 && GL <= 32, "head_dim must be 64, 128 or 256");
@@ -485,26 +485,12 @@ __global__ void __launch_bounds__(256, 2) score_stream_kernel(const ScoreDev a) 
     score_rows<T, D, METHOD>(a, r, gl, qs, raw);
   };
 
-  uint4 bufA[8], bufB[8];
-  SliceRef cur = locate_slice<D, PAGED>(a, cur_pos, grp);
-  issue_rows(a, cur, gl, bufA);
-  for (int64_t s = 0; s < count; s += 2) {
-    SliceRef nxt;
-    const bool has1 = s + 1 < count;
-    if (has1) {
-      cursor_next<RPW>(a, cur_pos);
-      nxt = locate_slice<D, PAGED>(a, cur_pos, grp);
-      issue_rows(a, nxt, gl, bufB);
-    }
-    score(cur, bufA);
-    if (!has1) break;
-    const bool has2 = s + 2 < count;
-    if (has2) {
-      cursor_next<RPW>(a, cur_pos);
-      cur = locate_slice<D, PAGED>(a, cur_pos, grp);
-      issue_rows(a, cur, gl, bufA);
-    }
-    score(nxt, bufB);
+  uint4 buf[8];
+  for (int64_t s = 0; s < count; ++s) {
+    if (s > 0) cursor_next<RPW>(a, cur_pos);
+    const SliceRef cur = locate_slice<D, PAGED>(a, cur_pos, grp);
+    issue_rows(a, cur, gl, buf);
+    score(cur, buf);
   }
   publish_scores(a);
 }
