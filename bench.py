@@ -271,8 +271,9 @@ def measured_peaks():
 NCU_TRAFFIC = {
     "gather": {"link_bytes": (1048576 + 65536) * 32,
                "source": "profiles/gather_decode_qwen7b.txt (move_rows_kernel<16>, ncu --set full)"},
-    "select": {"dram_bytes": 134962432 + 5281792 + 2126592,
-               "source": "profiles/select_decode_qwen7b.txt (score_stream_kernel + topk_smem_kernel<1>, ncu --set full)"},
+    "select": {"dram_bytes": 134341888 + 4309504 + 2133760,
+               "source": "profiles/select_decode_qwen7b.txt (score_stream_kernel, 24 warps per SM, + topk_smem_kernel<1> "
+                         "with the early stop, ncu --set full)"},
 }
 
 
