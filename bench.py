@@ -388,6 +388,26 @@ def workload_config(wl, name, world, plan_desc):
             "l2": f"inputs larger than L2: {wl['layers']} layers of HBM keys and host KV read per step"}
 
 
+def link_weighted_plan(wl, world, rank, h2d_ranks):
+    """This rank's share of the workload given every rank's concurrent H2D link rate (GB/s):
+    (plan, sequence-group weights or None, sequences per group, the job's GB/s bound).  With more
+    ranks than KV heads each sequence group takes sequences in proportion to the slowest rate
+    among its ranks (parallel.seq_split); the bound assumes every group's ranks move their share
+    at that rate, so the slowest group sets the step."""
+    from mserve_b200 import parallel
+    plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank)
+    rates = [min(h2d_ranks[r] for r in plan.group_ranks(g)) for g in range(plan.seq_groups)]
+    weights = None
+    if plan.seq_groups > 1:
+        weights = rates
+        plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank, seq_weights=weights)
+        counts = parallel.seq_split(wl["batch"], weights)
+    else:
+        counts = [wl["batch"]]
+    bound = wl["batch"] * plan.head_groups / max(n / r for n, r in zip(counts, rates))
+    return plan, weights, counts, bound
+
+
 def plan_description(wl, world):
     from mserve_b200.parallel import shard_plan
     p = shard_plan(wl["batch"], wl["kv_heads"], world, 0)
@@ -863,15 +883,7 @@ def run_mserve(args, world, rank, local):
     barrier(world)
     peaks = pcie_peaks(dev, world)
     h2d_ranks = gather_objects(peaks["h2d"], world)
-    plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank)
-    seq_weights = None
-    if plan.seq_groups > 1:
-        seq_weights = [min(h2d_ranks[r] for r in plan.group_ranks(g)) for g in range(plan.seq_groups)]
-        plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank, seq_weights=seq_weights)
-    seq_split_counts = (parallel.seq_split(wl["batch"], seq_weights) if seq_weights
-                        else [wl["batch"] // plan.seq_groups] * plan.seq_groups)
-    group_rates = seq_weights or [min(h2d_ranks[r] for r in plan.group_ranks(g)) for g in range(plan.seq_groups)]
-    split_bound_gbs = wl["batch"] * plan.head_groups / max(n / r for n, r in zip(seq_split_counts, group_rates))
+    plan, seq_weights, seq_split_counts, split_bound_gbs = link_weighted_plan(wl, world, rank, h2d_ranks)
     eng, q = build_engine(wl, plan, dev)
     eng.host_link_ctas = args.gather_ctas
     turn = None

@@ -95,3 +95,26 @@ def test_get_full_kv_host_tensors_and_oracle():
     np.testing.assert_array_equal(k.numpy(), ek)
     np.testing.assert_array_equal(v.numpy(), ev)
     assert CPUKVCache.get_full_kv(None, kn, vn) == (kn, vn)
+
+
+def test_link_weighted_plan():
+    """The bench's split of the 7B decode problem by measured link rates: even on equal links and
+    at N <= 4 (no sequence groups), 3 + 5 sequences when ranks 0-3 are slower at N = 8; the bound
+    is N x the slowest rate for even splits and the slowest group's rate otherwise."""
+    import bench
+    wl = dict(bench.WORKLOADS["qwen7b"][0])
+    plan, w, counts, bound = bench.link_weighted_plan(wl, 1, 0, [55.5])
+    assert w is None and counts == [8] and (plan.b0, plan.b1, plan.h0, plan.h1) == (0, 8, 0, 4)
+    assert bound == pytest.approx(55.5)
+    plan, w, counts, bound = bench.link_weighted_plan(wl, 4, 2, [28.7, 28.5, 28.9, 28.8])
+    assert w is None and counts == [8] and (plan.h0, plan.h1) == (2, 3) and bound == pytest.approx(4 * 28.5)
+    rates = [23.4, 23.4, 23.5, 23.5, 35.9, 36.2, 35.9, 35.8]
+    shares = {}
+    for r in range(8):
+        plan, w, counts, bound = bench.link_weighted_plan(wl, 8, r, rates)
+        assert w == [23.4, 35.8] and counts == [3, 5]
+        shares[r] = (plan.b0, plan.b1, plan.h0, plan.h1)
+        assert bound == pytest.approx(8 * 4 / max(3 / 23.4, 5 / 35.8))
+    assert shares[0] == (0, 3, 0, 1) and shares[7] == (3, 8, 3, 4)
+    plan, w, counts, _ = bench.link_weighted_plan(wl, 8, 5, [30.0] * 8)
+    assert counts == [4, 4] and (plan.b0, plan.b1) == (4, 8)
