@@ -390,34 +390,31 @@ def workload_config(wl, name, world, plan_desc):
 
 def link_weighted_plan(wl, world, rank, h2d_ranks):
     """This rank's share of the workload given every rank's concurrent H2D link rate (GB/s):
-    (plan, sequence-group weights or None, sequences per group, the job's GB/s bound).  With more
-    ranks than KV heads each sequence group takes sequences in proportion to the slowest rate
-    among its ranks (parallel.seq_split); the bound assumes every group's ranks move their share
-    at that rate, so the slowest group sets the step."""
+    (plan, sequence-group weights or None, sequences per group, the job's GB/s bound).  For
+    equal-length batches parallel.plan_for_links picks the head-group count and sizes each
+    sequence group by the slowest rate among its ranks; ragged batches keep the even split (the
+    bound then assumes every rank moves its share at the slowest rate)."""
     from mserve_b200 import parallel
+    if "lens_uniform" not in wl:
+        return parallel.plan_for_links(wl["batch"], wl["kv_heads"], world, rank, h2d_ranks)
     plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank)
-    rates = [min(h2d_ranks[r] for r in plan.group_ranks(g)) for g in range(plan.seq_groups)]
-    weights = None
-    if plan.seq_groups > 1:
-        weights = rates
-        plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank, seq_weights=weights)
-        counts = parallel.seq_split(wl["batch"], weights)
-    else:
-        counts = [wl["batch"]]
-    bound = wl["batch"] * plan.head_groups / max(n / r for n, r in zip(counts, rates))
-    return plan, weights, counts, bound
+    return plan, None, [wl["batch"] // plan.seq_groups] * plan.seq_groups, world * min(h2d_ranks)
 
 
 def plan_description(wl, world):
     from mserve_b200.parallel import shard_plan
     p = shard_plan(wl["batch"], wl["kv_heads"], world, 0)
-    if p.seq_groups == 1:
-        seqs = f"{p.b1 - p.b0} of {wl['batch']} sequences per rank"
-    else:
-        seqs = (f"the {wl['batch']} sequences over {p.seq_groups} sequence groups in proportion to each group's "
-                "slowest measured host-link rate (evenly when the links are equally fast)")
-    return (f"{world} rank(s) split one problem: {p.h1 - p.h0} of {wl['kv_heads']} KV heads x {seqs}, each rank "
-            "gathering over its own host link, no collective on the data path")
+    if world == 1:
+        return (f"1 rank: all {wl['kv_heads']} KV heads x {wl['batch']} sequences, gathering over its own host link")
+    if "lens_uniform" in wl:
+        return (f"{world} ranks split one problem: {p.h1 - p.h0} of {wl['kv_heads']} KV heads x {p.b1 - p.b0} of "
+                f"{wl['batch']} sequences per rank, each rank gathering over its own host link, no collective on "
+                "the data path")
+    return (f"{world} ranks split one problem over KV-head groups and sequence groups chosen from the ranks' "
+            f"measured concurrent host-link rates (by default {p.head_groups} head groups of {p.h1 - p.h0} of "
+            f"{wl['kv_heads']} KV heads, each sequence group taking sequences in proportion to its slowest link; "
+            "evenly when the links are equally fast), each rank gathering over its own host link, no collective on "
+            "the data path")
 
 
 # ------------------------------------------------------------------------------------- CPU path
@@ -759,13 +756,13 @@ def shared_selection_timing(wl, plan, eng, q, world, dev, L_time, reps=4):
     return res
 
 
-def extra_qwen32b(world, rank, dev, steps, warmup, chunks, layers=4):
-    """The Qwen2.5-VL-32B decode shape (16 x 32768 tokens, 40/8 heads, top-4096 + last 256), its
-    KV heads split over the ranks like the main workload, `layers` of its 64 layers: whole-job
+def extra_qwen32b(world, rank, dev, steps, warmup, chunks, h2d_ranks, layers=4):
+    """The Qwen2.5-VL-32B decode shape (16 x 32768 tokens, 40/8 heads, top-4096 + last 256), split
+    over the ranks like the main workload (link_weighted_plan), `layers` of its 64 layers: whole-job
     GB/s and step ms (max over ranks) of the captured step."""
-    from mserve_b200 import ops, parallel
+    from mserve_b200 import ops
     wl = dict(WORKLOADS["qwen32b"][0], layers=layers)
-    plan = parallel.shard_plan(wl["batch"], wl["kv_heads"], world, rank)
+    plan, _, counts, _ = link_weighted_plan(wl, world, rank, h2d_ranks)
     eng, q = build_engine(wl, plan, dev)
     out = torch.empty((wl["layers"],) + tuple(eng.buffers().out.shape), dtype=eng.dtype, device=dev)
     g = eng.capture_decode_step(q, out, chunks=chunks)
@@ -787,7 +784,8 @@ def extra_qwen32b(world, rank, dev, steps, warmup, chunks, layers=4):
     torch.cuda.empty_cache()
     return {"value": total / t / 1e9, "unit": "GB/s", "ms_per_step": t / steps * 1e3, "layers": wl["layers"],
             "of_layers": 64, "steps": steps,
-            "shard": {"kv_heads_per_rank": plan.h1 - plan.h0, "sequences_per_rank": plan.b1 - plan.b0},
+            "shard": {"kv_heads_per_rank": plan.h1 - plan.h0, "sequences_per_rank": plan.b1 - plan.b0,
+                      "head_groups": plan.head_groups, "sequences_per_group": counts},
             "workload": WORKLOADS["qwen32b"][1] + f" ({layers} of its 64 layers)"}
 
 
@@ -1009,7 +1007,7 @@ def run_mserve(args, world, rank, local):
     # The 32B shape, the 34B multi-turn shape and transfer-sweep points on the same ranks.
     extra = None
     if not args.no_extra:
-        extra = {"qwen32b_decode": extra_qwen32b(world, rank, dev, args.steps, args.warmup, args.chunks),
+        extra = {"qwen32b_decode": extra_qwen32b(world, rank, dev, args.steps, args.warmup, args.chunks, h2d_ranks),
                  "llava34b_decode": extra_llava34b(world, rank, dev, args.steps, args.warmup, args.chunks),
                  "transfer": extra_transfer_points(world, dev, peaks_all)}
 

@@ -89,18 +89,20 @@ def seq_split(batch: int, weights) -> list:
     return n
 
 
-def shard_plan(batch: int, kv_heads: int, world: int, rank: int, seq_weights=None) -> ShardPlan:
+def shard_plan(batch: int, kv_heads: int, world: int, rank: int, seq_weights=None,
+               head_groups: Optional[int] = None) -> ShardPlan:
     """Splits batch x kv_heads (sequence, KV head) pairs over `world` ranks (see ShardPlan).
 
-    The KV heads always split evenly.  When there are more ranks than KV heads the sequences are
-    split too: evenly, or, with seq_weights (one relative rate per sequence group, e.g. the
-    slowest measured host-link rate among the group's ranks), by seq_split so that groups on
-    faster links take more sequences.  Every rank must pass the same weights."""
+    The KV heads always split evenly, over head_groups groups (default min(world, kv_heads)).
+    When there are more ranks than head groups the sequences are split too: evenly, or, with
+    seq_weights (one relative rate per sequence group, e.g. the slowest measured host-link rate
+    among the group's ranks), by seq_split so that groups on faster links take more sequences.
+    Every rank must pass the same arguments."""
     if world <= 0 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} of world {world}")
-    hg = min(world, kv_heads)
-    if kv_heads % hg or world % hg:
-        raise ValueError(f"{world} ranks cannot split {kv_heads} KV heads evenly")
+    hg = min(world, kv_heads) if head_groups is None else int(head_groups)
+    if hg <= 0 or kv_heads % hg or world % hg:
+        raise ValueError(f"{world} ranks cannot split {kv_heads} KV heads evenly over {hg} head groups")
     sg = world // hg
     hl = kv_heads // hg
     hi, si = rank % hg, rank // hg
@@ -117,6 +119,38 @@ def shard_plan(batch: int, kv_heads: int, world: int, rank: int, seq_weights=Non
         b0 = sum(counts[:si])
         b1 = b0 + counts[si]
     return ShardPlan(world, rank, hg, sg, b0, b1, hi * hl, (hi + 1) * hl)
+
+
+def plan_for_links(batch: int, kv_heads: int, world: int, rank: int, rates, min_gain: float = 0.03):
+    """The split of batch x kv_heads (sequence, KV head) pairs of equal-length sequences over
+    `world` ranks whose host links move `rates[r]` (e.g. GB/s, measured with all ranks copying at
+    once).  Every head-group count hg that divides kv_heads and world is tried: sequence group g
+    (ranks g*hg .. g*hg + hg - 1) moves at its slowest rank's rate, takes seq_split's share of the
+    sequences (all of them with one group), and the group with the longest time sets the step.
+    The default plan (hg = min(world, kv_heads), sequence groups weighted) is kept unless another
+    hg is faster by more than min_gain.  Returns (plan, seq_weights or None, sequences per group,
+    bound), bound being the job's rate in the units of `rates`.  Every rank must pass the same
+    rates."""
+    if len(rates) != world:
+        raise ValueError(f"{len(rates)} link rates for {world} ranks")
+
+    def evaluate(hg):
+        sg = world // hg
+        w = [min(rates[r] for r in range(g * hg, (g + 1) * hg)) for g in range(sg)]
+        counts = seq_split(batch, w) if sg > 1 else [batch]
+        step = max(n * (kv_heads // hg) / r for n, r in zip(counts, w))
+        return (w if sg > 1 else None), counts, batch * kv_heads / step
+
+    default = min(world, kv_heads)
+    best = (default,) + evaluate(default)
+    for hg in range(default - 1, 0, -1):
+        if kv_heads % hg or world % hg or batch < world // hg:
+            continue
+        cand = (hg,) + evaluate(hg)
+        if cand[3] > best[3] * (1.0 + min_gain):
+            best = cand
+    hg, weights, counts, bound = best
+    return shard_plan(batch, kv_heads, world, rank, seq_weights=weights, head_groups=hg), weights, counts, bound
 
 
 def exchange_head_scores(local: torch.Tensor, gathered: torch.Tensor, group=None) -> torch.Tensor:

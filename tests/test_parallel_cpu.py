@@ -333,3 +333,41 @@ def test_weighted_shard_plan_covers_every_pair_once(rates):
     assert shard_plan(8, 4, 4, 1, seq_weights=[9.0]) == shard_plan(8, 4, 4, 1)
     with pytest.raises(ValueError):
         shard_plan(B, Hkv, world, 0, seq_weights=[1.0, 2.0, 3.0])
+
+
+def test_plan_for_links_picks_head_groups_by_link_rates():
+    """Equal links keep the default plan; uneven links move to fewer head groups only when the
+    bound improves by more than 3%; every (sequence, KV head) pair stays on exactly one rank and
+    the ranks of a sequence group hold the same sequences."""
+    from mserve_b200.parallel import plan_for_links, shard_plan
+    slow_fast = [23.4, 23.4, 23.5, 23.5, 35.9, 36.2, 35.9, 35.8]
+    cases = [  # batch, kv heads, world, rates, expected head groups, sequences per group
+        (16, 8, 8, [30.0] * 8, 8, [16]),
+        (16, 8, 8, slow_fast, 4, [6, 10]),
+        (8, 4, 8, slow_fast, 4, [3, 5]),
+        (8, 4, 4, [23.0, 23.0, 36.0, 36.0], 2, [3, 5]),
+        (8, 4, 4, [28.7, 28.5, 28.9, 28.8], 4, [8]),
+        (8, 4, 2, [55.5, 55.4], 2, [8]),
+    ]
+    for B, H, world, rates, hg, counts in cases:
+        owner = {}
+        bounds = set()
+        for r in range(world):
+            plan, w, c, bound = plan_for_links(B, H, world, r, rates)
+            assert plan.head_groups == hg and c == counts, (B, H, world, rates, plan, c)
+            assert (w is None) == (len(counts) == 1)
+            bounds.add(round(bound, 9))
+            for q in plan.group_ranks(plan.seq_group):
+                o = plan_for_links(B, H, world, q, rates)[0]
+                assert (o.b0, o.b1) == (plan.b0, plan.b1)
+            for b in range(plan.b0, plan.b1):
+                for h in range(plan.h0, plan.h1):
+                    assert (b, h) not in owner
+                    owner[(b, h)] = r
+        assert len(owner) == B * H and len(bounds) == 1
+    # the default plan's bound is world x the slowest rate for equal shares
+    _, _, _, bound = plan_for_links(16, 8, 8, 0, [30.0] * 8)
+    assert bound == pytest.approx(240.0)
+    assert shard_plan(16, 8, 8, 0, head_groups=4, seq_weights=[1.0, 1.0]).b1 == 8
+    with pytest.raises(ValueError):
+        plan_for_links(8, 4, 8, 0, [1.0] * 4)
