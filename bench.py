@@ -12,7 +12,8 @@ attention over them.
 N ranks (torchrun, one per GPU) split this one problem: the KV heads first, then the sequences
 when there are more ranks than KV heads (mserve_b200.parallel.shard_plan), each sequence group
 taking sequences in proportion to the slowest concurrent host-link rate among its ranks, measured
-at start-up (evenly when the links are equally fast).  Every rank holds its
+at start-up (evenly when the links are equally fast); parallel.plan_for_links groups the KV heads
+more coarsely instead when the measured rates make that more than 3% faster.  Every rank holds its
 (sequence, KV head) pairs in its own host store and gathers them over its own host link; there
 is no collective on the data path ("scaling": "strong": the total work is fixed).  The KV and
 queries of every (layer, sequence, head) come from their own seed, so each N computes exactly the
