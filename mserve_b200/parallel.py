@@ -3,7 +3,9 @@
 One process per GPU; rank r holds the KV heads [r*Hl, (r+1)*Hl) of every sequence, Hl =
 Hkv / world, in its own host store, and gathers them over its own host link.  With more ranks
 than KV heads the sequences are split too (shard_plan): every (sequence, KV head) pair lives on
-exactly one rank.
+exactly one rank.  Host links differ in what they sustain when every GPU pulls at once, so the
+sequences can be shared out by measured link rate (seq_split), and plan_for_links picks the
+head-group count and the sequence shares that finish soonest for given per-rank rates.
 
 * Per-(sequence, KV head) selection (the recent-window top-k) needs no exchange: each rank
   scores, selects, gathers and attends its own heads, and nothing crosses NVLink.
